@@ -1,0 +1,501 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 row-reduction backend (one JSON line on stdout).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+                    [--workload NAME] [--headline-only]
+
+Metric: achieved HBM GB/s (algorithmic bytes: inputs read once + outputs
+written once) per kernel, as a fraction of the measured B200 copy bandwidth,
+with E_lib = t_torch / t_cuda * 100 against the torch GPU operator.
+
+A step is one launch of the op over one batch of a workload. The headline
+workload is the RMSNorm bf16 [16384, 8192] configuration; every other
+configuration is timed too and reported under "kernels". Under torchrun each
+rank runs on its own GPU: the headline and the single-GPU workloads are
+replicated per rank (weak scaling), the row-sharded LayerNorm is split into
+row blocks (strong scaling); there is no collective on the data path (NCCL
+only carries the max-over-ranks of the timings).
+
+Timing: W untimed warm-up steps, then exactly K steps; before each step a
+512 MiB buffer is written (L2 flush, and it keeps the GPU busy while the host
+enqueues the step); each step is bracketed by CUDA events on the launching
+stream. The K-step region is bracketed by a barrier and device synchronise;
+the reported time is the max over ranks. SM clocks and throttle reasons are
+sampled (NVML, read-only) during the timed regions.
+
+--impl reference times the CPU implementation of the same path (the oracle
+restatement of the reference's pytorch_impl, all host threads) on a bounded
+sample of the same workload; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from dslperfgap_b200 import workloads  # noqa: E402
+
+METRIC = "HBM GB/s and % of B200 peak per kernel at 1/2/4/8 GPUs; E_lib vs torch"
+HEADLINE = "rms_norm_bf16"
+SPEC_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+FLUSH_BYTES = 512 << 20
+SHORT = {torch.float32: "fp32", torch.float16: "fp16", torch.bfloat16: "bf16"}
+
+
+# --------------------------------------------------------------------------- env
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch from a committed ncu summary, if present."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return {}
+    return {}
+
+
+# ------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML (read-only)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.active = False
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = index
+            if visible:
+                ids = [v.strip() for v in visible.split(",") if v.strip()]
+                if index < len(ids) and ids[index].isdigit():
+                    phys = int(ids[index])
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report no clocks
+            self._nv = None
+            self.error = str(e)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            if self.active:
+                try:
+                    self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                    for bit, name in self.REASONS.items():
+                        if r & bit and bit != 0x1:
+                            self.reasons.add(name)
+                except Exception as e:
+                    self.error = str(e)
+            time.sleep(self.period)
+
+    period = 0.005
+
+    def start(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=2)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0, "note": self.error or "no samples"}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------ timing
+class Timer:
+    def __init__(self, device, world):
+        self.device = device
+        self.world = world
+        self.flush_buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def flush(self):
+        self.flush_buf.fill_(1.0)
+
+    def barrier(self):
+        if self.world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(self.device)
+
+    def time_steps(self, fn, steps, warmup, sampler=None):
+        """Run fn warmup + steps times; return per-step device ms list (this rank)."""
+        for _ in range(warmup):
+            self.flush()
+            fn()
+        torch.cuda.synchronize(self.device)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        self.barrier()
+        if sampler:
+            sampler.active = True
+        for i in range(steps):
+            self.flush()
+            starts[i].record()
+            fn()
+            ends[i].record()
+        torch.cuda.synchronize(self.device)
+        if sampler:
+            sampler.active = False
+        self.barrier()
+        return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+    def max_over_ranks(self, value: float) -> float:
+        if self.world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+
+# --------------------------------------------------------------- direct launches
+def direct_launcher(wl, dev):
+    """Closure calling the C ABI on preallocated buffers (the kernel alone)."""
+    from dslperfgap_b200 import _lib
+    lib = _lib.load()
+    cfg = wl.config
+    code = _lib.FLOAT_CODES[cfg.dtype]
+    a = wl.args
+    M, N = wl.M, cfg.N
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    keep = []
+    if cfg.op == "layer_norm":
+        y = torch.empty_like(a[0])
+        keep = [y]
+        f = lambda: lib.dslpg_layer_norm_fwd(a[0].data_ptr(), a[1].data_ptr(), a[2].data_ptr(), y.data_ptr(), M, N,
+                                             code, code, 1e-5, stream)
+    elif cfg.op == "rms_norm":
+        y = torch.empty_like(a[0])
+        keep = [y]
+        eps = wl.kwargs.get("eps", 1e-5)
+        f = lambda: lib.dslpg_rms_norm_fwd(a[0].data_ptr(), a[2].data_ptr(), y.data_ptr(), M, N, code, code, eps,
+                                           stream)
+    elif cfg.op == "softmax":
+        y = torch.empty_like(a[0])
+        keep = [y]
+        f = lambda: lib.dslpg_softmax_fwd(a[0].data_ptr(), y.data_ptr(), M, N, code, stream)
+    elif cfg.op == "log_softmax":
+        y = torch.empty_like(a[0])
+        keep = [y]
+        f = lambda: lib.dslpg_log_softmax_fwd(a[0].data_ptr(), y.data_ptr(), M, N, 1, code, code, stream)
+    elif cfg.op == "logsumexp":
+        y = torch.empty(M, dtype=cfg.dtype, device=dev)
+        keep = [y]
+        f = lambda: lib.dslpg_logsumexp_fwd(a[0].data_ptr(), y.data_ptr(), M, N, code, stream)
+    elif cfg.op == "cross_entropy":
+        k = wl.kwargs
+        # The kernel writes the M valid entries of each output; the wrapper's
+        # [M, N] allocations only add address space, so they are not needed here.
+        outs = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(3)]
+        keep = outs
+        f = lambda: lib.dslpg_cross_entropy_fwd(
+            a[0].data_ptr(), a[1].data_ptr(), outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(), M, N, N,
+            code, _lib.I64, k["smoothing"], k["logit_scale"], k["lse_square_scale"], k["ignored_index"],
+            float(k["total_classes"]), k["class_start_idx"], k["BLOCK_SIZE"], 0, 0, stream)
+    else:
+        raise KeyError(cfg.op)
+
+    def call():
+        rc = f()
+        if rc != 0:
+            raise RuntimeError(f"{cfg.op}: {_lib.load().dslpg_error_string(rc).decode()}")
+    call.keep = keep
+    return call
+
+
+def torch_baseline(wl):
+    """The torch GPU operator E_lib is computed against (the reference's library baselines)."""
+    import torch.nn.functional as F
+    cfg, a, kw = wl.config, wl.args, wl.kwargs
+    if cfg.op == "layer_norm":
+        return "F.layer_norm", lambda: F.layer_norm(a[0], (cfg.N,), a[1], a[2], 1e-5)
+    if cfg.op == "rms_norm":
+        return "F.rms_norm", lambda: F.rms_norm(a[0], (cfg.N,), a[2], kw.get("eps", 1e-5))
+    if cfg.op == "softmax":
+        return "F.softmax", lambda: F.softmax(a[0], -1)
+    if cfg.op == "log_softmax":
+        return "F.log_softmax", lambda: F.log_softmax(a[0], -1)
+    if cfg.op == "logsumexp":
+        return "torch.logsumexp", lambda: torch.logsumexp(a[0], -1)
+    if cfg.op == "cross_entropy":
+        return "F.cross_entropy(mean)", lambda: F.cross_entropy(a[0], a[1], ignore_index=-100)
+    raise KeyError(cfg.op)
+
+
+def eager_reference_expression(wl):
+    """The reference's pytorch_impl computation written as eager torch (RMSNorm only:
+    pytorch_impl.rms_norm is 5 kernels, the other pytorch_impls are one torch op)."""
+    if wl.config.op != "rms_norm":
+        return None
+    x, w, eps = wl.args[0], wl.args[2], wl.kwargs.get("eps", 1e-5)
+    return lambda: ((x.float() / torch.sqrt(torch.mean(x.float() ** 2, dim=-1, keepdim=True) + eps))
+                    * w.float()).to(x.dtype)
+
+
+# ------------------------------------------------------------------ measurements
+def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler, with_torch=True):
+    cfg = workloads.CONFIGS[name]
+    sharded = name == "layer_norm_bf16_sharded"
+    rows = workloads.shard_rows(cfg.M, rank, world) if sharded else None
+    wl = workloads.make(name, seed=0, device=dev, rows=rows)
+    launch = direct_launcher(wl, dev)
+    per = timer.time_steps(launch, steps, warmup, sampler)
+    local_total = sum(per)
+    t_max = timer.max_over_ranks(local_total)
+    bytes_rank = wl.algo_bytes()
+    total_rows = cfg.M if sharded else cfg.M * world
+    total_bytes = workloads.algo_bytes(cfg, total_rows) * steps
+    ms_step = t_max / steps
+    agg_gbs = total_bytes / (t_max * 1e-3) / 1e9
+    kernel_ms = statistics.mean(per)
+    achieved = bytes_rank / (kernel_ms * 1e-3) / 1e9
+    res = {
+        "shape": [wl.M, cfg.N], "dtype": SHORT[cfg.dtype], "rows_per_gpu": wl.M,
+        "scaling": "strong" if sharded else "weak",
+        "ms_per_step": round(ms_step, 5), "median_ms": round(statistics.median(per), 5),
+        "gbs": round(agg_gbs, 1), "gbs_per_gpu": round(achieved, 1),
+        "frac_measured": round(achieved / peak, 4), "frac_spec": round(achieved / SPEC_HBM_GBS, 4),
+        "algo_bytes_per_launch": bytes_rank, "launches": steps,
+    }
+    if with_torch:
+        label, fn = torch_baseline(wl)
+        try:
+            tp = timer.time_steps(fn, steps, warmup)
+            t_torch = timer.max_over_ranks(sum(tp)) / steps
+            res["torch_op"] = label
+            res["torch_ms"] = round(t_torch, 5)
+            res["e_lib_pct"] = round(100.0 * t_torch / ms_step, 1)
+        except Exception as e:  # report, do not hide
+            res["torch_error"] = f"{type(e).__name__}: {e}"[:200]
+        eager = eager_reference_expression(wl)
+        if eager is not None:
+            te = timer.time_steps(eager, steps, warmup)
+            t_e = timer.max_over_ranks(sum(te)) / steps
+            res["torch_eager_pytorch_impl_ms"] = round(t_e, 5)
+            res["e_lib_vs_pytorch_impl_pct"] = round(100.0 * t_e / ms_step, 1)
+    del launch, wl
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_e2e(name, rank, world, dev, timer, steps, warmup):
+    """Same metric through the public API with pinned host buffers: per step the
+    step's input goes host->device, the op runs, the result comes back."""
+    import dslperfgap_b200 as B
+    cfg = workloads.CONFIGS[name]
+    wl = workloads.make(name, seed=0, device=dev)
+    x_host = wl.args[0].cpu().pin_memory()
+    w = wl.args[2]
+    x_dev = torch.empty_like(wl.args[0])
+    y_host = torch.empty_like(x_host).pin_memory()
+    eps = wl.kwargs.get("eps", 1e-5)
+
+    def step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = B.rms_norm(x_dev, (cfg.N,), w, eps=eps)
+        y_host.copy_(y, non_blocking=True)
+
+    per = timer.time_steps(step, steps, warmup)
+    t_max = timer.max_over_ranks(sum(per))
+    total = workloads.algo_bytes(cfg, cfg.M) * world * steps
+    return {"value": round(total / (t_max * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+            "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
+            "ms_per_step": round(t_max / steps, 4), "path": "dslperfgap_b200.rms_norm (public API), pinned host buffers"}
+
+
+# ----------------------------------------------------------------- CPU baseline
+def cpu_sample(name, target_s=1.0):
+    """Time the oracle (all host threads) on a bounded row sample; returns dict."""
+    from oracle import oracle
+    cfg = workloads.CONFIGS[name]
+    fn = getattr(oracle, cfg.fn_name)
+    rows = max(1, min(cfg.M, (1 << 20) // cfg.N))
+    wl = workloads.make(name, seed=0, device="cpu", rows=(0, rows))
+    t0 = time.perf_counter()
+    fn(*wl.args, **wl.kwargs)
+    dt = time.perf_counter() - t0
+    rows = max(1, min(cfg.M, int(rows * target_s / max(dt, 1e-6))))
+    wl = workloads.make(name, seed=0, device="cpu", rows=(0, rows))
+    return wl, fn
+
+
+def run_cpu_baseline(name, seconds=10.0):
+    from oracle import oracle
+    wl, fn = cpu_sample(name, target_s=seconds / 5)
+    fn(*wl.args, **wl.kwargs)  # warm
+    times = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        fn(*wl.args, **wl.kwargs)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    gbs = wl.algo_bytes() / t / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": oracle.threads(), "kind": "port",
+            "sample": f"{wl.M} of {wl.config.M} rows of {name} ({wl.algo_bytes()} algorithmic bytes), median of 5 "
+                      f"calls of the C oracle (restatement of ViperBench/{wl.config.op}/pytorch_impl.py), "
+                      f"{oracle.threads()} host threads"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the CPU implementation of the path on the host cores."""
+    if rank != 0:
+        return 0
+    from oracle import oracle
+    name = args.workload
+    cfg = workloads.CONFIGS[name]
+    wl, fn = cpu_sample(name, target_s=0.25)
+    for _ in range(args.warmup):
+        fn(*wl.args, **wl.kwargs)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn(*wl.args, **wl.kwargs)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    gbs = wl.algo_bytes() * args.steps / total / 1e9
+    sample = (f"{wl.M} of {cfg.M} rows of {name} per step; C oracle restating "
+              f"ViperBench/{cfg.op}/pytorch_impl.py, {oracle.threads()} host threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": SHORT[cfg.dtype],
+        "data": "synthetic (seeded, BASELINE distributions)",
+        "config": workloads.config_dict(cfg),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": oracle.threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# -------------------------------------------------------------------------- main
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--workload", default=HEADLINE, choices=workloads.NAMES)
+    ap.add_argument("--headline-only", action="store_true", help="skip the other configurations")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = dist_env()
+
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}))
+        return 1
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=dev)
+    import dslperfgap_b200._lib as L
+    L.load()  # fails loudly when the CUDA library is not built
+
+    peak, peak_kind = measured_peak()
+    timer = Timer(dev, world)
+    sampler = ClockSampler(local)
+    sampler.start()
+
+    head = measure_workload(args.workload, rank, world, dev, timer, args.steps, args.warmup, peak, sampler)
+    kernels = {args.workload: head}
+    if not args.headline_only:
+        for name in workloads.NAMES:
+            if name != args.workload:
+                kernels[name] = measure_workload(name, rank, world, dev, timer, args.steps, args.warmup, peak,
+                                                 sampler)
+    e2e = measure_e2e(HEADLINE, rank, world, dev, timer, max(3, min(args.steps, 20)), args.warmup) \
+        if args.workload == HEADLINE else None
+    sampler.stop()
+    clocks = sampler.summary()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = run_cpu_baseline(args.workload, args.cpu_seconds)
+
+    if world > 1:
+        torch.distributed.barrier()
+    if rank == 0:
+        cfg = workloads.CONFIGS[args.workload]
+        traffic = profile_traffic().get(args.workload)
+        line = {
+            "metric": METRIC, "value": head["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": head["scaling"], "vs_baseline": None, "dtype": SHORT[cfg.dtype],
+            "data": "synthetic (seeded generators with the BASELINE shapes and distributions)",
+            "config": {**workloads.config_dict(cfg), "l2": "512 MiB buffer written between timed steps",
+                       "parallelism": f"row-independent; {world} rank(s), one per GPU, no data-path collective"},
+            "roofline": {"bound": "hbm", "achieved": head["gbs_per_gpu"], "peak": peak, "unit": "GB/s",
+                         "frac": round(head["gbs_per_gpu"] / peak, 4),
+                         "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                         "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6.65 TB/s"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": sum(k["launches"] for k in kernels.values()) + (e2e and max(3, min(args.steps, 20)) or 0),
+            "clocks": clocks,
+            "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,15 @@
+"""B200 (sm_100a) CUDA backend for DSLPerfGap's ViperBench row-reduction family.
+
+``dslperfgap_b200.<kernel>.cuda_impl`` mirrors ``ViperBench/<kernel>/cuda_impl.py``
+of the reference suite: the same function names and signatures as its
+pytorch/triton/tilelang backends, running hand-written sm_100a kernels from
+``lib/libdslpg_b200.so`` through the C ABI declared in ``include/dslpg_b200.h``.
+"""
+from .layer_norm.cuda_impl import layer_norm
+from .rms_norm.cuda_impl import rms_norm
+from .softmax.cuda_impl import softmax
+from .log_softmax.cuda_impl import log_softmax
+from .logsumexp.cuda_impl import logsumexp
+from .cross_entropy.cuda_impl import cross_entropy_fwd
+
+__all__ = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy_fwd"]

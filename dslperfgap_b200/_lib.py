@@ -1,0 +1,99 @@
+"""ctypes binding of the C ABI in ``include/dslpg_b200.h``.
+
+This is the only place Python touches the native library. There is no CPU
+implementation behind it: if ``lib/libdslpg_b200.so`` is missing, or a tensor
+is not on a CUDA device, the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libdslpg_b200.so"
+
+F32, F16, BF16, I32, I64 = 0, 1, 2, 3, 4
+FLOAT_CODES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+LABEL_CODES = {torch.int32: I32, torch.int64: I64}
+
+_c_i64 = ctypes.c_int64
+_c_int = ctypes.c_int
+_c_f32 = ctypes.c_float
+_vp = ctypes.c_void_p
+
+# name -> argtypes (every entry point returns int)
+SIGNATURES = {
+    "dslpg_layer_norm_fwd": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_f32, _vp],
+    "dslpg_rms_norm_fwd": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_f32, _vp],
+    "dslpg_softmax_fwd": [_vp, _vp, _c_i64, _c_i64, _c_int, _vp],
+    "dslpg_log_softmax_fwd": [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
+    "dslpg_logsumexp_fwd": [_vp, _vp, _c_i64, _c_i64, _c_int, _vp],
+    "dslpg_cross_entropy_fwd": [
+        _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
+        _c_f32, _c_f32, _c_f32, _c_i64, _c_f32, _c_i64, _c_i64, _c_int, _c_int, _vp,
+    ],
+    "dslpg_version": [],
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the native library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"dslperfgap_b200: CUDA library {LIB_PATH} is not built; run "
+                    "`python -m dslperfgap_b200.build` (there is no CPU fallback)"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, argtypes in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = ctypes.c_int
+            lib.dslpg_error_string.argtypes = [ctypes.c_int]
+            lib.dslpg_error_string.restype = ctypes.c_char_p
+            _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().dslpg_error_string(rc).decode()
+        raise RuntimeError(f"{what} failed ({rc}): {msg}")
+
+
+def float_code(t: torch.Tensor, what: str) -> int:
+    code = FLOAT_CODES.get(t.dtype)
+    if code is None:
+        raise TypeError(f"{what}: unsupported dtype {t.dtype}; expected float32, float16 or bfloat16")
+    return code
+
+
+def require_cuda(*tensors, what: str) -> torch.device:
+    """All tensors must live on the same CUDA device; return it."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{what}: expected a torch.Tensor, got {type(t).__name__}")
+        if t.device.type != "cuda":
+            raise ValueError(f"{what}: tensors must be on a CUDA device (got {t.device}); "
+                             "this backend has no CPU path")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"{what}: tensors are on different devices ({dev} and {t.device})")
+    return dev
+
+
+def stream_handle(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream

@@ -1,0 +1,110 @@
+"""Build recipe for the CUDA C-ABI library ``lib/libdslpg_b200.so``.
+
+The library is compiled in-tree with nvcc for sm_100a only:
+each ``csrc/*.cu`` becomes an object (in parallel), and the objects are linked
+into one shared library against the CUDA runtime. Re-running is cheap: an
+object is rebuilt only when a source or header under ``csrc/`` or ``include/``
+is newer than it.
+
+Usage: ``python -m dslperfgap_b200.build [--force] [--verbose]``
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+REPO_DIR = PKG_DIR.parent
+CSRC = PKG_DIR / "csrc"
+INCLUDE = REPO_DIR / "include"
+BUILD_DIR = PKG_DIR / "_build"
+LIB_DIR = PKG_DIR / "lib"
+LIB_NAME = "libdslpg_b200.so"
+LIB_PATH = LIB_DIR / LIB_NAME
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-lineinfo",
+    "-Xcompiler", "-fPIC",
+    "-Xcompiler", "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+    "-DDSLPG_BUILD",
+]
+
+
+def nvcc_path() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: set NVCC or put /usr/local/cuda/bin on PATH")
+
+
+def _newest_header_mtime() -> float:
+    mt = 0.0
+    for p in list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h")):
+        mt = max(mt, p.stat().st_mtime)
+    return mt
+
+
+def _compile(src: Path, obj: Path, extra: list[str], verbose: bool) -> None:
+    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, *extra, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name}:\n{res.stdout}\n{res.stderr}")
+    if verbose and (res.stdout or res.stderr):
+        print(res.stdout + res.stderr, flush=True)
+
+
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
+    """Compile every csrc/*.cu for sm_100a and link lib/libdslpg_b200.so."""
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    sources = sorted(CSRC.glob("*.cu"))
+    hdr_mt = _newest_header_mtime()
+    extra = ["-Xptxas", "-v"] if ptxas_info else []
+    todo = []
+    objs = []
+    for src in sources:
+        obj = BUILD_DIR / (src.stem + ".o")
+        objs.append(obj)
+        stale = force or ptxas_info or not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, hdr_mt)
+        if stale:
+            todo.append((src, obj))
+    if todo:
+        with cf.ThreadPoolExecutor(max_workers=min(len(todo), os.cpu_count() or 4)) as ex:
+            futs = [ex.submit(_compile, s, o, extra, verbose or ptxas_info) for s, o in todo]
+            for f in futs:
+                f.result()
+    relink = bool(todo) or not LIB_PATH.exists() or any(o.stat().st_mtime > LIB_PATH.stat().st_mtime for o in objs)
+    if relink:
+        tmp = LIB_DIR / (LIB_NAME + ".tmp")
+        cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+        os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--ptxas-info", action="store_true", help="print -Xptxas -v register/spill info")
+    args = ap.parse_args(argv)
+    path = build(force=args.force, verbose=args.verbose, ptxas_info=args.ptxas_info)
+    print(path)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

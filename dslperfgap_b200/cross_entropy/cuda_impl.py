@@ -1,0 +1,52 @@
+"""CUDA (sm_100a) backend of ViperBench ``cross_entropy`` (forward).
+
+Same signature as ViperBench/cross_entropy/pytorch_impl.py:4-90::
+
+    cross_entropy_fwd(logits, labels, smoothing, logit_scale, lse_square_scale,
+                      ignored_index, total_classes, class_start_idx, BLOCK_SIZE,
+                      HAS_SMOOTHING, SPLIT) -> (loss, lse, z_loss)
+
+Each output is a float32 tensor of shape [n_rows, n_cols] in the kernel layout
+of ViperBench/cross_entropy/triton_impl.py:123-140: the value for row r and
+column block cb sits at flat index cb * n_rows + r, for
+cb < ceil(n_cols / BLOCK_SIZE). As with the Triton backend the outputs are
+allocated with torch.empty, so flat entries past the valid range are not
+written (pytorch_impl zero-fills them). Under SPLIT the z_loss entries are 0.
+"""
+import torch
+
+from .. import _lib
+
+
+def cross_entropy_fwd(
+    logits, labels, smoothing, logit_scale, lse_square_scale,
+    ignored_index, total_classes, class_start_idx, BLOCK_SIZE, HAS_SMOOTHING, SPLIT
+):
+    dev = _lib.require_cuda(logits, labels, what="cross_entropy_fwd")
+    lcode = _lib.float_code(logits, "cross_entropy_fwd logits")
+    if logits.dim() != 2:
+        raise ValueError(f"cross_entropy_fwd: logits must be 2-D, got shape {tuple(logits.shape)}")
+    if labels.dtype not in _lib.LABEL_CODES:
+        raise TypeError(f"cross_entropy_fwd: labels must be int32 or int64, got {labels.dtype}")
+    n_rows, n_cols = logits.shape
+    if labels.dim() != 1 or labels.shape[0] != n_rows:
+        raise ValueError(f"cross_entropy_fwd: labels shape {tuple(labels.shape)} != ({n_rows},)")
+    if int(BLOCK_SIZE) <= 0:
+        raise ValueError(f"cross_entropy_fwd: BLOCK_SIZE must be positive, got {BLOCK_SIZE}")
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    labels = labels.contiguous()
+    loss = torch.empty((n_rows, n_cols), dtype=torch.float32, device=logits.device)
+    lse = torch.empty((n_rows, n_cols), dtype=torch.float32, device=logits.device)
+    z_loss = torch.empty((n_rows, n_cols), dtype=torch.float32, device=logits.device)
+    if n_rows == 0 or n_cols == 0:
+        return loss, lse, z_loss
+    with torch.cuda.device(dev):
+        rc = _lib.load().dslpg_cross_entropy_fwd(
+            logits.data_ptr(), labels.data_ptr(), loss.data_ptr(), lse.data_ptr(), z_loss.data_ptr(),
+            n_rows, n_cols, logits.stride(0), lcode, _lib.LABEL_CODES[labels.dtype],
+            float(smoothing), float(logit_scale), float(lse_square_scale), int(ignored_index),
+            float(total_classes), int(class_start_idx), int(BLOCK_SIZE),
+            1 if HAS_SMOOTHING else 0, 1 if SPLIT else 0, _lib.stream_handle(dev))
+    _lib.check(rc, "dslpg_cross_entropy_fwd")
+    return loss, lse, z_loss

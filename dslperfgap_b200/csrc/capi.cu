@@ -1,0 +1,82 @@
+// capi.cu — library-wide C entry points and the host launch helpers.
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace dslpg {
+
+namespace {
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];  // 0 = not queried yet
+
+struct OccKey {
+  int dev;
+  const void* fn;
+  int block;
+  size_t smem;
+  bool operator==(const OccKey& o) const {
+    return dev == o.dev && fn == o.fn && block == o.block && smem == o.smem;
+  }
+};
+struct OccKeyHash {
+  size_t operator()(const OccKey& k) const {
+    size_t h = std::hash<const void*>()(k.fn);
+    h ^= (static_cast<size_t>(k.dev) << 1) ^ (static_cast<size_t>(k.block) << 9) ^ (k.smem << 21);
+    return h;
+  }
+};
+std::mutex g_occ_mu;
+std::unordered_map<OccKey, int, OccKeyHash> g_occ;
+}  // namespace
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int n = g_sm_count[dev];
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    g_sm_count[dev] = n;  // benign race: every writer stores the same value
+  }
+  return n;
+}
+
+int persistent_grid(const void* kernel, int block, size_t smem, int64_t work_ctas) {
+  if (work_ctas <= 0) return 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int occ = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    auto it = g_occ.find(OccKey{dev, kernel, block, smem});
+    if (it != g_occ.end()) occ = it->second;
+  }
+  if (occ == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, block, smem) != cudaSuccess ||
+        occ <= 0)
+      occ = 1;
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    g_occ[OccKey{dev, kernel, block, smem}] = occ;
+  }
+  int64_t full = static_cast<int64_t>(occ) * sm_count();
+  return static_cast<int>(work_ctas < full ? work_ctas : full);
+}
+
+}  // namespace dslpg
+
+extern "C" int dslpg_version(void) { return (0 << 16) | 1; }
+
+extern "C" const char* dslpg_error_string(int code) {
+  switch (code) {
+    case DSLPG_OK: return "success";
+    case DSLPG_ERR_NULL_POINTER: return "dslpg: a required pointer is NULL";
+    case DSLPG_ERR_BAD_SHAPE: return "dslpg: invalid shape (sizes must be positive and in range)";
+    case DSLPG_ERR_BAD_DTYPE: return "dslpg: unsupported dtype code";
+    case DSLPG_ERR_BAD_EPS: return "dslpg: eps must be finite and >= 0";
+    case DSLPG_ERR_BAD_ARGUMENT: return "dslpg: invalid argument";
+    default: break;
+  }
+  if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
+  return "dslpg: unknown error";
+}

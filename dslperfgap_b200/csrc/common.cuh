@@ -1,0 +1,223 @@
+// common.cuh — shared device helpers for the row-reduction kernels (sm_100a).
+//
+// Everything here is memory-movement and reduction plumbing: 16-byte vector
+// loads and stores with cache hints, fp16/bf16 <-> fp32 unpacking, NaN-
+// propagating max, warp and row-group reductions, and the host-side launch
+// helpers (SM count, occupancy-sized persistent grids).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/dslpg_b200.h"
+
+#define DSLPG_DEV __device__ __forceinline__
+
+namespace dslpg {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.69314718055994531f;
+constexpr float kNegInf = -__builtin_huge_valf();
+constexpr float kPosInf = __builtin_huge_valf();
+
+// ----------------------------------------------------------------------------
+// Storage types
+// ----------------------------------------------------------------------------
+struct alignas(16) Vec16 {
+  uint32_t w[4];
+};
+
+template <typename T> struct Elt;
+template <> struct Elt<float> { static constexpr int kPerVec = 4; };
+template <> struct Elt<__half> { static constexpr int kPerVec = 8; };
+template <> struct Elt<__nv_bfloat16> { static constexpr int kPerVec = 8; };
+
+DSLPG_DEV float to_f(float v) { return v; }
+DSLPG_DEV float to_f(__half v) { return __half2float(v); }
+DSLPG_DEV float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> DSLPG_DEV T from_f(float v);
+template <> DSLPG_DEV float from_f<float>(float v) { return v; }
+template <> DSLPG_DEV __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <> DSLPG_DEV __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Round v to T's precision and back (exact when T is fp32).
+template <typename T> DSLPG_DEV float round_to(float v) { return to_f(from_f<T>(v)); }
+
+// Scalar load of element i of an array whose dtype is only known at run time.
+DSLPG_DEV float load_any(const void* p, int64_t i, int dt) {
+  if (dt == DSLPG_F32) return __ldg(static_cast<const float*>(p) + i);
+  if (dt == DSLPG_F16) return __half2float(__ldg(static_cast<const __half*>(p) + i));
+  return __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p) + i));
+}
+
+// ----------------------------------------------------------------------------
+// Vector memory ops
+// ----------------------------------------------------------------------------
+// Read-once activations: do not allocate in L1 (the row is read once from HBM).
+DSLPG_DEV Vec16 ld_stream(const void* p) {
+  Vec16 v;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+      : "l"(p));
+  return v;
+}
+
+// Data re-read by many rows (weight / bias vectors): keep in L1.
+DSLPG_DEV Vec16 ld_keep(const void* p) {
+  Vec16 v;
+  asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+      : "l"(p));
+  return v;
+}
+
+DSLPG_DEV void st_stream(void* p, const Vec16& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+               "r"(v.w[2]), "r"(v.w[3])
+               : "memory");
+}
+
+DSLPG_DEV void st_stream8(void* p, uint32_t a, uint32_t b) {
+  asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+
+// Unpack one 16-byte vector of T into fp32 (Elt<T>::kPerVec values).
+template <typename T> DSLPG_DEV void unpack(const Vec16& v, float* f);
+template <> DSLPG_DEV void unpack<float>(const Vec16& v, float* f) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = __uint_as_float(v.w[i]);
+}
+template <> DSLPG_DEV void unpack<__nv_bfloat16>(const Vec16& v, float* f) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(v.w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(v.w[i] & 0xffff0000u);
+  }
+}
+template <> DSLPG_DEV void unpack<__half>(const Vec16& v, float* f) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&v.w[i]);
+    float2 t = __half22float2(h);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// Pack two fp32 values into one 32-bit word of T (T 16-bit), round to nearest even.
+template <typename T> DSLPG_DEV uint32_t pack2(float a, float b);
+template <> DSLPG_DEV uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <> DSLPG_DEV uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Store E fp32 values as E elements of T at p (p aligned to E * sizeof(T)).
+// E is 4 or 8; the store is 8, 16 or 32 bytes.
+template <typename T, int E> struct StoreOut;
+template <int E> struct StoreOut<float, E> {
+  static DSLPG_DEV void run(void* p, const float* f) {
+#pragma unroll
+    for (int q = 0; q < E / 4; ++q) {
+      Vec16 v;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v.w[i] = __float_as_uint(f[4 * q + i]);
+      st_stream(static_cast<char*>(p) + 16 * q, v);
+    }
+  }
+};
+template <typename T16> struct Store16Bit {
+  template <int E> static DSLPG_DEV void run(void* p, const float* f) {
+    if constexpr (E == 4) {
+      st_stream8(p, pack2<T16>(f[0], f[1]), pack2<T16>(f[2], f[3]));
+    } else {
+      Vec16 v;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v.w[i] = pack2<T16>(f[2 * i], f[2 * i + 1]);
+      st_stream(p, v);
+    }
+  }
+};
+template <int E> struct StoreOut<__half, E> {
+  static DSLPG_DEV void run(void* p, const float* f) { Store16Bit<__half>::run<E>(p, f); }
+};
+template <int E> struct StoreOut<__nv_bfloat16, E> {
+  static DSLPG_DEV void run(void* p, const float* f) { Store16Bit<__nv_bfloat16>::run<E>(p, f); }
+};
+
+// ----------------------------------------------------------------------------
+// Arithmetic
+// ----------------------------------------------------------------------------
+// 2^x on the SFU; x = -inf gives 0, NaN stays NaN. Results below 2^-126 flush
+// to zero, which only drops terms < 1e-38 relative to the largest one.
+DSLPG_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// exp(d) for d = x - max (d <= 0 in normal use).
+DSLPG_DEV float exp_shifted(float d) { return ex2(d * kLog2e); }
+
+// max that returns NaN when either operand is NaN (torch's amax semantics).
+DSLPG_DEV float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+struct SumOp {
+  static DSLPG_DEV float identity() { return 0.f; }
+  static DSLPG_DEV float apply(float a, float b) { return a + b; }
+};
+struct MaxOp {
+  static DSLPG_DEV float identity() { return kNegInf; }
+  static DSLPG_DEV float apply(float a, float b) { return max_nan(a, b); }
+};
+
+// Butterfly reduction: every lane ends with the same bits.
+template <class Op> DSLPG_DEV float warp_reduce(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = Op::apply(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Reduction over a row group of `nw` consecutive warps (group g of the CTA).
+// `red` is a 32-float shared buffer indexed by the CTA's warp number. All
+// threads of the CTA must call this (it contains a __syncthreads when nw > 1).
+// Alternate between two buffers for back-to-back reductions: a buffer may be
+// rewritten only after the next barrier.
+template <class Op>
+DSLPG_DEV float group_reduce(float v, float* red, int nw, int first_warp) {
+  v = warp_reduce<Op>(v);
+  if (nw == 1) return v;
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = lane < nw ? red[first_warp + lane] : Op::identity();
+  return warp_reduce<Op>(r);
+}
+
+// ----------------------------------------------------------------------------
+// Host helpers
+// ----------------------------------------------------------------------------
+// SM count of the current device (cached per device).
+int sm_count();
+
+// Persistent grid: enough CTAs to fill every SM at full occupancy, but no more
+// than there is work for. `kernel` is the kernel's host stub.
+int persistent_grid(const void* kernel, int block, size_t smem, int64_t work_ctas);
+
+inline int dtype_size(int dt) { return dt == DSLPG_F32 ? 4 : 2; }
+inline bool is_float_dtype(int dt) { return dt == DSLPG_F32 || dt == DSLPG_F16 || dt == DSLPG_BF16; }
+inline bool aligned(const void* p, int bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(bytes)) == 0;
+}
+
+}  // namespace dslpg

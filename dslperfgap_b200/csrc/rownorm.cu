@@ -1,0 +1,706 @@
+// rownorm.cu — row-normalising kernels: layer_norm, rms_norm, softmax,
+// log_softmax (sm_100a).
+//
+// All four read a row, reduce it to one or two statistics, and write a row of
+// the same length. Three kernel shapes cover every input:
+//
+//  * resident_kernel: the row is split over a group of `tpr` threads (a warp
+//    for short rows, up to a 1024-thread CTA for 128 KiB rows), each holding
+//    VPT 16-byte vectors in registers. HBM is read once and written once; the
+//    statistics are warp-shuffle + shared-memory reductions. Used whenever the
+//    row is 16-byte vectorisable and fits (<= 8192 vectors).
+//  * stream_kernel: one CTA per row, two passes. Pass 1 streams the row into
+//    per-thread online statistics (Welford / running max+sum); pass 2 re-reads
+//    the row (an L2 hit: a CTA's row is at most a few hundred KiB) and writes
+//    the output. Used for rows too long for registers and for unaligned or
+//    odd-length rows (scalar variant).
+//  * strided_log_softmax_kernel: log_softmax over a non-last dim of an
+//    [M, N, K] tensor; each thread owns one (m, k) column, reads are coalesced
+//    across k.
+//
+// Numerics: fp32 accumulation, one rounding at the store, NaN-propagating max
+// (torch semantics: a NaN anywhere in a softmax row poisons the row).
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace dslpg {
+
+enum RowOp : int { kLayerNorm = 0, kRmsNorm = 1, kSoftmax = 2, kLogSoftmax = 3 };
+
+struct RowArgs {
+  const void* x;
+  void* y;
+  const void* w;  // layer_norm / rms_norm weight [N] (dtype wdt)
+  const void* b;  // layer_norm bias [N] (dtype wdt) or nullptr
+  int64_t M;
+  int N;
+  int nvec;   // N / elements-per-vector (vector paths)
+  int tpr;    // threads per row
+  int rpc;    // rows per CTA (resident kernel)
+  float eps;
+  int wdt;    // weight dtype code
+  int wvec;   // 1: weight/bias have x's dtype and are 16-byte aligned
+};
+
+// log_softmax(x, dtype=Tout) first converts x to Tout (a no-op when Tout is fp32).
+template <typename Tin, typename Tout>
+constexpr bool kRoundIn = !std::is_same<Tin, Tout>::value && !std::is_same<Tout, float>::value;
+
+template <typename Tin, typename Tout>
+DSLPG_DEV float in_value(float v) {
+  if constexpr (kRoundIn<Tin, Tout>) return round_to<Tout>(v);
+  return v;
+}
+
+// Weight (and bias) elements [j*E, j*E+E) as fp32. The resident kernel is only
+// used when weight and bias have x's dtype and are 16-byte aligned.
+template <typename Tin, int E>
+DSLPG_DEV void load_weight(const void* p, int j, float* out) {
+  if (p == nullptr) {
+#pragma unroll
+    for (int i = 0; i < E; ++i) out[i] = 0.f;
+    return;
+  }
+  unpack<Tin>(ld_keep(static_cast<const Tin*>(p) + static_cast<int64_t>(j) * E), out);
+}
+
+// ============================================================================
+// Resident kernel
+// ============================================================================
+template <int OP, typename Tin, typename Tout, int VPT>
+__global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
+  constexpr int E = Elt<Tin>::kPerVec;
+  // Up to 16 fp32 values per thread are kept unpacked (softmax keeps the exp
+  // values there, so each element costs one ex2); longer slices stay packed and
+  // are unpacked again in each phase.
+  constexpr bool kCache = VPT * E <= 16;
+  // With <= 4 vectors per thread the next row's vectors are loaded before this
+  // row is reduced, so every thread always has loads in flight.
+  constexpr bool kPrefetch = VPT <= 4;
+  __shared__ float red[2][32];
+
+  const int g = threadIdx.x / a.tpr;
+  const int t = threadIdx.x - g * a.tpr;
+  const int nw = a.tpr >> 5;
+  const int first_warp = g * nw;
+  const float n_f = static_cast<float>(a.N);
+  int buf = 0;
+
+  auto load_row = [&](Vec16* dst, int64_t row) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int j = t + k * a.tpr;
+      dst[k] = Vec16{{0u, 0u, 0u, 0u}};
+      if (row < a.M && j < a.nvec)
+        dst[k] = ld_stream(static_cast<const Tin*>(a.x) + row * a.N + static_cast<int64_t>(j) * E);
+    }
+  };
+
+  const int64_t step = static_cast<int64_t>(gridDim.x) * a.rpc;
+  Vec16 nxt[kPrefetch ? VPT : 1];
+  if constexpr (kPrefetch) load_row(nxt, static_cast<int64_t>(blockIdx.x) * a.rpc + g);
+
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * a.rpc; base < a.M; base += step) {
+    const int64_t row = base + g;
+    Tout* yr = static_cast<Tout*>(a.y) + row * a.N;
+
+    Vec16 v[VPT];
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) v[k] = nxt[k];
+      load_row(nxt, row + step);
+    } else {
+      load_row(v, row);
+    }
+    bool ok[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) ok[k] = row < a.M && (t + k * a.tpr) < a.nvec;
+
+    float fr[kCache ? VPT : 1][E];
+    if constexpr (kCache) {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        unpack<Tin>(v[k], fr[k]);
+#pragma unroll
+        for (int i = 0; i < E; ++i) fr[k][i] = in_value<Tin, Tout>(fr[k][i]);
+      }
+    }
+    // The fp32 values of vector k (masked vectors read as 0).
+    auto get = [&](int k, float* f) {
+      if constexpr (kCache) {
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = fr[k][i];
+      } else {
+        unpack<Tin>(v[k], f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
+      }
+    };
+
+    if constexpr (OP == kRmsNorm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        float f[E];
+        get(k, f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) ss = fmaf(f[i], f[i], ss);
+      }
+      ss = group_reduce<SumOp>(ss, red[buf], nw, first_warp);
+      buf ^= 1;
+      const float inv = 1.0f / sqrtf(ss / n_f + a.eps);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        const int j = t + k * a.tpr;
+        float f[E], w[E];
+        get(k, f);
+        load_weight<Tin, E>(a.w, j, w);
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = (f[i] * inv) * w[i];
+        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+      }
+    } else if constexpr (OP == kLayerNorm) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        float f[E];
+        get(k, f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) s += f[i];
+      }
+      s = group_reduce<SumOp>(s, red[buf], nw, first_warp);
+      buf ^= 1;
+      const float mean = s / n_f;
+      float q = 0.f;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        float f[E];
+        get(k, f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          const float d = f[i] - mean;
+          q = fmaf(d, d, q);
+        }
+      }
+      q = group_reduce<SumOp>(q, red[buf], nw, first_warp);
+      buf ^= 1;
+      const float rstd = 1.0f / sqrtf(q / n_f + a.eps);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        const int j = t + k * a.tpr;
+        float f[E], w[E], bb[E];
+        get(k, f);
+        load_weight<Tin, E>(a.w, j, w);
+        load_weight<Tin, E>(a.b, j, bb);
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - mean) * rstd, w[i], bb[i]);
+        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+      }
+    } else {  // kSoftmax / kLogSoftmax
+      float m = kNegInf;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        float f[E];
+        get(k, f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) m = max_nan(m, f[i]);
+      }
+      m = group_reduce<MaxOp>(m, red[buf], nw, first_warp);
+      buf ^= 1;
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        float f[E];
+        get(k, f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          const float e = exp_shifted(f[i] - m);
+          if constexpr (kCache && OP == kSoftmax) fr[k][i] = e;
+          s += e;
+        }
+      }
+      s = group_reduce<SumOp>(s, red[buf], nw, first_warp);
+      buf ^= 1;
+      if constexpr (OP == kSoftmax) {
+        const float inv = 1.0f / s;
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          if (!ok[k]) continue;
+          const int j = t + k * a.tpr;
+          float f[E];
+          if constexpr (kCache) {
+#pragma unroll
+            for (int i = 0; i < E; ++i) f[i] = fr[k][i] * inv;
+          } else {
+            get(k, f);
+#pragma unroll
+            for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - m) * inv;
+          }
+          StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+        }
+      } else {
+        const float ls = logf(s);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+          if (!ok[k]) continue;
+          const int j = t + k * a.tpr;
+          float f[E];
+          get(k, f);
+#pragma unroll
+          for (int i = 0; i < E; ++i) f[i] = (f[i] - m) - ls;
+          StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+        }
+      }
+    }
+  }
+}
+
+// ============================================================================
+// Stream kernel (two passes; any length and alignment)
+// ============================================================================
+// Running statistics of one thread.
+struct Welford {
+  float n, mean, m2;
+};
+
+DSLPG_DEV Welford welford_merge(Welford a, Welford b) {
+  const float n = a.n + b.n;
+  if (n == 0.f) return a;
+  const float d = b.mean - a.mean;
+  const float fb = b.n / n;
+  Welford r;
+  r.n = n;
+  r.mean = a.mean + d * fb;
+  r.m2 = a.m2 + b.m2 + d * d * a.n * fb;
+  return r;
+}
+
+// Online max / sum-of-exp update with a chunk of values (invalid ones are -inf).
+DSLPG_DEV void online_update(float& m, float& s, const float* f, int n) {
+  float cm = kNegInf;
+  for (int i = 0; i < n; ++i) cm = max_nan(cm, f[i]);
+  const float nm = max_nan(m, cm);
+  if (nm == kNegInf) return;  // every value so far is -inf: nothing to add
+  s = (m == nm) ? s : s * exp_shifted(m - nm);
+  for (int i = 0; i < n; ++i) s += exp_shifted(f[i] - nm);
+  m = nm;
+}
+
+// Combine (max, sum) pairs of one row spread over the CTA; returns the row's.
+DSLPG_DEV void block_merge_ms(float& m, float& s, float* red0, float* red1) {
+  const int nw = blockDim.x >> 5;
+  const float gm = group_reduce<MaxOp>(m, red0, nw, 0);
+  const float sc = (m == gm) ? s : s * exp_shifted(m - gm);
+  s = group_reduce<SumOp>(sc, red1, nw, 0);
+  m = gm;
+}
+
+DSLPG_DEV Welford warp_merge_welford(Welford w) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Welford other;
+    other.n = __shfl_down_sync(0xffffffffu, w.n, o);
+    other.mean = __shfl_down_sync(0xffffffffu, w.mean, o);
+    other.m2 = __shfl_down_sync(0xffffffffu, w.m2, o);
+    w = welford_merge(w, other);
+  }
+  // lane 0 holds the warp's statistics; broadcast them.
+  w.n = __shfl_sync(0xffffffffu, w.n, 0);
+  w.mean = __shfl_sync(0xffffffffu, w.mean, 0);
+  w.m2 = __shfl_sync(0xffffffffu, w.m2, 0);
+  return w;
+}
+
+DSLPG_DEV Welford block_merge_welford(Welford w, float* sh /* [3][32] */) {
+  w = warp_merge_welford(w);
+  const int nw = blockDim.x >> 5;
+  if (nw == 1) return w;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) {
+    sh[wid] = w.n;
+    sh[32 + wid] = w.mean;
+    sh[64 + wid] = w.m2;
+  }
+  __syncthreads();
+  Welford r{0.f, 0.f, 0.f};
+  if (lane < nw) r = Welford{sh[lane], sh[32 + lane], sh[64 + lane]};
+  r = warp_merge_welford(r);
+  __syncthreads();  // sh may be reused by the caller's next row
+  return r;
+}
+
+template <typename Tin, int V>
+DSLPG_DEV void load_unit(const Tin* xr, int j, bool ok, float* f) {
+  if constexpr (V == 1) {
+    f[0] = ok ? to_f(xr[j]) : 0.f;
+  } else {
+    Vec16 v{{0u, 0u, 0u, 0u}};
+    if (ok) v = ld_stream(xr + static_cast<int64_t>(j) * V);
+    unpack<Tin>(v, f);
+  }
+}
+
+template <typename Tin, int V>
+DSLPG_DEV void load_weight_unit(const RowArgs& a, const void* p, int j, float* w) {
+  if (p == nullptr) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) w[i] = 0.f;
+  } else if (V > 1 && a.wvec) {
+    load_weight<Tin, V>(p, j, w);
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) w[i] = load_any(p, static_cast<int64_t>(j) * V + i, a.wdt);
+  }
+}
+
+template <typename Tout, int V>
+DSLPG_DEV void store_unit(Tout* yr, int j, const float* f) {
+  if constexpr (V == 1) {
+    yr[j] = from_f<Tout>(f[0]);
+  } else {
+    StoreOut<Tout, V>::run(yr + static_cast<int64_t>(j) * V, f);
+  }
+}
+
+template <int OP, typename Tin, typename Tout, int V>
+__global__ void __launch_bounds__(1024) stream_kernel(const RowArgs a) {
+  constexpr int U = 4;  // units in flight per thread per iteration
+  __shared__ float sh[3][32];
+  __shared__ float sh_w[96];
+  const int t = threadIdx.x;
+  const int tpr = blockDim.x;
+  const int units = (V == 1) ? a.N : a.nvec;
+  const float n_f = static_cast<float>(a.N);
+
+  for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x) {
+    const Tin* xr = static_cast<const Tin*>(a.x) + row * a.N;
+    Tout* yr = static_cast<Tout*>(a.y) + row * a.N;
+
+    // ---- pass 1: statistics
+    float ss = 0.f;                 // rms_norm
+    Welford wf{0.f, 0.f, 0.f};      // layer_norm
+    float m = kNegInf, s = 0.f;     // softmax family
+    for (int j0 = t; j0 < units; j0 += U * tpr) {
+      float f[U][V];
+      bool ok[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + u * tpr;
+        ok[u] = j < units;
+        load_unit<Tin, V>(xr, j, ok[u], f[u]);
+#pragma unroll
+        for (int i = 0; i < V; ++i) f[u][i] = in_value<Tin, Tout>(f[u][i]);
+      }
+      if constexpr (OP == kRmsNorm) {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int i = 0; i < V; ++i) ss = fmaf(f[u][i], f[u][i], ss);
+      } else if constexpr (OP == kLayerNorm) {
+        float c = 0.f, cs = 0.f;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (!ok[u]) continue;
+          c += V;
+#pragma unroll
+          for (int i = 0; i < V; ++i) cs += f[u][i];
+        }
+        if (c > 0.f) {
+          const float cmean = cs / c;
+          float cm2 = 0.f;
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            if (!ok[u]) continue;
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              const float d = f[u][i] - cmean;
+              cm2 = fmaf(d, d, cm2);
+            }
+          }
+          wf = welford_merge(wf, Welford{c, cmean, cm2});
+        }
+      } else {
+        float flat[U * V];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int i = 0; i < V; ++i) flat[u * V + i] = ok[u] ? f[u][i] : kNegInf;
+        online_update(m, s, flat, U * V);
+      }
+    }
+
+    // ---- combine across the CTA
+    float p0 = 0.f, p1 = 0.f;  // per-op parameters of pass 2
+    if constexpr (OP == kRmsNorm) {
+      ss = group_reduce<SumOp>(ss, sh[0], tpr >> 5, 0);
+      p0 = 1.0f / sqrtf(ss / n_f + a.eps);
+    } else if constexpr (OP == kLayerNorm) {
+      wf = block_merge_welford(wf, sh_w);
+      p0 = wf.mean;
+      p1 = 1.0f / sqrtf(wf.m2 / n_f + a.eps);
+    } else {
+      block_merge_ms(m, s, sh[0], sh[1]);
+      if (!(fabsf(m) < kPosInf)) s = __int_as_float(0x7fc00000);  // non-finite max: NaN row
+      p0 = m;
+      p1 = (OP == kSoftmax) ? 1.0f / s : logf(s);
+    }
+
+    // ---- pass 2: output (re-read; the row is L2-resident)
+    for (int j0 = t; j0 < units; j0 += U * tpr) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + u * tpr;
+        if (j >= units) continue;
+        float f[V];
+        load_unit<Tin, V>(xr, j, true, f);
+#pragma unroll
+        for (int i = 0; i < V; ++i) f[i] = in_value<Tin, Tout>(f[i]);
+        if constexpr (OP == kRmsNorm) {
+          float w[V];
+          load_weight_unit<Tin, V>(a, a.w, j, w);
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[i] = (f[i] * p0) * w[i];
+        } else if constexpr (OP == kLayerNorm) {
+          float w[V], bb[V];
+          load_weight_unit<Tin, V>(a, a.w, j, w);
+          load_weight_unit<Tin, V>(a, a.b, j, bb);
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[i] = fmaf((f[i] - p0) * p1, w[i], bb[i]);
+        } else if constexpr (OP == kSoftmax) {
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[i] = exp_shifted(f[i] - p0) * p1;
+        } else {
+#pragma unroll
+          for (int i = 0; i < V; ++i) f[i] = (f[i] - p0) - p1;
+        }
+        store_unit<Tout, V>(yr, j, f);
+      }
+    }
+    __syncthreads();  // shared buffers are reused by the next row
+  }
+}
+
+// ============================================================================
+// log_softmax over the middle axis of [M, N, K]
+// ============================================================================
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(256) strided_log_softmax_kernel(const Tin* __restrict__ x,
+                                                                  Tout* __restrict__ y, int64_t M,
+                                                                  int64_t N, int64_t K) {
+  const int64_t cols = M * K;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < cols;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t mi = c / K;
+    const int64_t k = c - mi * K;
+    const Tin* xc = x + mi * N * K + k;
+    Tout* yc = y + mi * N * K + k;
+    float m = kNegInf, s = 0.f;
+    for (int64_t n = 0; n < N; ++n) {
+      float f = in_value<Tin, Tout>(to_f(xc[n * K]));
+      online_update(m, s, &f, 1);
+    }
+    if (!(fabsf(m) < kPosInf)) s = __int_as_float(0x7fc00000);
+    const float ls = logf(s);
+    for (int64_t n = 0; n < N; ++n) {
+      const float f = in_value<Tin, Tout>(to_f(xc[n * K]));
+      yc[n * K] = from_f<Tout>((f - m) - ls);
+    }
+  }
+}
+
+// ============================================================================
+// Host dispatch
+// ============================================================================
+namespace {
+
+inline int round_up32(int v) { return (v + 31) & ~31; }
+
+template <int OP, typename Tin, typename Tout, int VPT>
+cudaError_t launch_resident(RowArgs a, cudaStream_t st) {
+  a.tpr = round_up32((a.nvec + VPT - 1) / VPT);
+  a.rpc = a.tpr >= 256 ? 1 : 256 / a.tpr;
+  const int block = a.tpr * a.rpc;
+  const void* fn = reinterpret_cast<const void*>(&resident_kernel<OP, Tin, Tout, VPT>);
+  const int grid = persistent_grid(fn, block, 0, (a.M + a.rpc - 1) / a.rpc);
+  resident_kernel<OP, Tin, Tout, VPT><<<grid, block, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int OP, typename Tin, typename Tout, int V>
+cudaError_t launch_stream(RowArgs a, cudaStream_t st) {
+  const int units = V == 1 ? a.N : a.nvec;
+  int block = round_up32((units + 3) / 4);
+  block = block < 32 ? 32 : (block > 1024 ? 1024 : block);
+  a.tpr = block;
+  a.rpc = 1;
+  const void* fn = reinterpret_cast<const void*>(&stream_kernel<OP, Tin, Tout, V>);
+  const int grid = persistent_grid(fn, block, 0, a.M);
+  stream_kernel<OP, Tin, Tout, V><<<grid, block, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// Largest row (in 16-byte vectors) kept in registers: 128 KiB of fp32 (8 vectors
+// per thread over 1024 threads) or 64 KiB of 16-bit data (4 vectors per thread;
+// 8 packed 16-bit vectors per thread do not fit the 64-register budget).
+
+template <int OP, typename Tin, typename Tout>
+cudaError_t dispatch_rows(RowArgs a, cudaStream_t st) {
+  constexpr int E = Elt<Tin>::kPerVec;
+  const bool vec = (a.N % E == 0) && aligned(a.x, 16) &&
+                   aligned(a.y, E * static_cast<int>(sizeof(Tout)));
+  if (vec) {
+    a.nvec = a.N / E;
+    const bool weights_ok = (OP != kLayerNorm && OP != kRmsNorm) || a.wvec;
+    const int max_resident = (E == 4) ? 8192 : 4096;
+    if (a.nvec <= max_resident && weights_ok) {
+      // About 16 elements per thread (4 fp32 or 2 16-bit vectors), more only
+      // when the row would need more than 1024 threads, fewer for short rows.
+      constexpr int kBase = (E == 4) ? 4 : 2;
+      if constexpr (E == 4) {
+        if (a.nvec > 4 * 1024) return launch_resident<OP, Tin, Tout, 8>(a, st);
+      }
+      if (a.nvec > kBase * 1024) return launch_resident<OP, Tin, Tout, 4>(a, st);
+      if (a.nvec >= 32 * kBase) return launch_resident<OP, Tin, Tout, kBase>(a, st);
+      if (a.nvec > 32) return launch_resident<OP, Tin, Tout, 2>(a, st);
+      return launch_resident<OP, Tin, Tout, 1>(a, st);
+    }
+    return launch_stream<OP, Tin, Tout, E>(a, st);
+  }
+  a.nvec = 0;
+  return launch_stream<OP, Tin, Tout, 1>(a, st);
+}
+
+template <int OP, typename Tin>
+cudaError_t dispatch_out(RowArgs a, int out_dt, cudaStream_t st) {
+  switch (out_dt) {
+    case DSLPG_F32: return dispatch_rows<OP, Tin, float>(a, st);
+    case DSLPG_F16: return dispatch_rows<OP, Tin, __half>(a, st);
+    default: return dispatch_rows<OP, Tin, __nv_bfloat16>(a, st);
+  }
+}
+
+template <int OP>
+cudaError_t dispatch_in(RowArgs a, int in_dt, int out_dt, cudaStream_t st) {
+  switch (in_dt) {
+    case DSLPG_F32: return dispatch_out<OP, float>(a, out_dt, st);
+    case DSLPG_F16: return dispatch_out<OP, __half>(a, out_dt, st);
+    default: return dispatch_out<OP, __nv_bfloat16>(a, out_dt, st);
+  }
+}
+
+// Same-dtype ops only instantiate the diagonal.
+template <int OP>
+cudaError_t dispatch_same(RowArgs a, int dt, cudaStream_t st) {
+  switch (dt) {
+    case DSLPG_F32: return dispatch_rows<OP, float, float>(a, st);
+    case DSLPG_F16: return dispatch_rows<OP, __half, __half>(a, st);
+    default: return dispatch_rows<OP, __nv_bfloat16, __nv_bfloat16>(a, st);
+  }
+}
+
+int check_rows(const void* x, const void* y, int64_t M, int64_t N) {
+  if (x == nullptr || y == nullptr) return DSLPG_ERR_NULL_POINTER;
+  if (M < 0 || N < 0 || N > 0x7fffffff) return DSLPG_ERR_BAD_SHAPE;
+  return DSLPG_OK;
+}
+
+RowArgs make_args(const void* x, void* y, const void* w, const void* b, int64_t M, int64_t N,
+                  int x_dt, int w_dt, float eps) {
+  RowArgs a{};
+  a.x = x;
+  a.y = y;
+  a.w = w;
+  a.b = b;
+  a.M = M;
+  a.N = static_cast<int>(N);
+  a.eps = eps;
+  a.wdt = w_dt;
+  a.wvec = (w != nullptr && w_dt == x_dt && aligned(w, 16) && (b == nullptr || aligned(b, 16)))
+               ? 1
+               : 0;
+  return a;
+}
+
+}  // namespace
+}  // namespace dslpg
+
+using namespace dslpg;
+
+extern "C" int dslpg_layer_norm_fwd(const void* x, const void* weight, const void* bias, void* y,
+                                    int64_t M, int64_t N, int x_dtype, int w_dtype, float eps,
+                                    cudaStream_t stream) {
+  if (int rc = check_rows(x, y, M, N)) return rc;
+  if (weight == nullptr) return DSLPG_ERR_NULL_POINTER;
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(w_dtype)) return DSLPG_ERR_BAD_DTYPE;
+  if (!(eps >= 0.f) || !(eps < kPosInf)) return DSLPG_ERR_BAD_EPS;
+  if (M == 0 || N == 0) return DSLPG_OK;
+  RowArgs a = make_args(x, y, weight, bias, M, N, x_dtype, w_dtype, eps);
+  return static_cast<int>(dispatch_same<kLayerNorm>(a, x_dtype, stream));
+}
+
+extern "C" int dslpg_rms_norm_fwd(const void* x, const void* weight, void* y, int64_t M, int64_t N,
+                                  int x_dtype, int w_dtype, float eps, cudaStream_t stream) {
+  if (int rc = check_rows(x, y, M, N)) return rc;
+  if (weight == nullptr) return DSLPG_ERR_NULL_POINTER;
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(w_dtype)) return DSLPG_ERR_BAD_DTYPE;
+  if (!(eps >= 0.f) || !(eps < kPosInf)) return DSLPG_ERR_BAD_EPS;
+  if (M == 0 || N == 0) return DSLPG_OK;
+  RowArgs a = make_args(x, y, weight, nullptr, M, N, x_dtype, w_dtype, eps);
+  return static_cast<int>(dispatch_same<kRmsNorm>(a, x_dtype, stream));
+}
+
+extern "C" int dslpg_softmax_fwd(const void* x, void* y, int64_t M, int64_t N, int dtype,
+                                 cudaStream_t stream) {
+  if (int rc = check_rows(x, y, M, N)) return rc;
+  if (!is_float_dtype(dtype)) return DSLPG_ERR_BAD_DTYPE;
+  if (M == 0 || N == 0) return DSLPG_OK;
+  RowArgs a = make_args(x, y, nullptr, nullptr, M, N, dtype, dtype, 0.f);
+  return static_cast<int>(dispatch_same<kSoftmax>(a, dtype, stream));
+}
+
+namespace {
+template <typename Tin, typename Tout>
+cudaError_t launch_strided(const void* x, void* y, int64_t M, int64_t N, int64_t K,
+                           cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&strided_log_softmax_kernel<Tin, Tout>);
+  const int64_t cols = M * K;
+  const int grid = persistent_grid(fn, 256, 0, (cols + 255) / 256);
+  strided_log_softmax_kernel<Tin, Tout><<<grid, 256, 0, st>>>(static_cast<const Tin*>(x),
+                                                              static_cast<Tout*>(y), M, N, K);
+  return cudaGetLastError();
+}
+template <typename Tin>
+cudaError_t strided_out(const void* x, void* y, int64_t M, int64_t N, int64_t K, int out_dt,
+                        cudaStream_t st) {
+  switch (out_dt) {
+    case DSLPG_F32: return launch_strided<Tin, float>(x, y, M, N, K, st);
+    case DSLPG_F16: return launch_strided<Tin, __half>(x, y, M, N, K, st);
+    default: return launch_strided<Tin, __nv_bfloat16>(x, y, M, N, K, st);
+  }
+}
+}  // namespace
+
+extern "C" int dslpg_log_softmax_fwd(const void* x, void* y, int64_t M, int64_t N, int64_t K,
+                                     int in_dtype, int out_dtype, cudaStream_t stream) {
+  if (int rc = check_rows(x, y, M, N)) return rc;
+  if (K < 1) return DSLPG_ERR_BAD_SHAPE;
+  if (!is_float_dtype(in_dtype) || !is_float_dtype(out_dtype)) return DSLPG_ERR_BAD_DTYPE;
+  if (M == 0 || N == 0) return DSLPG_OK;
+  if (K == 1) {
+    RowArgs a = make_args(x, y, nullptr, nullptr, M, N, in_dtype, in_dtype, 0.f);
+    return static_cast<int>(dispatch_in<kLogSoftmax>(a, in_dtype, out_dtype, stream));
+  }
+  cudaError_t e;
+  switch (in_dtype) {
+    case DSLPG_F32: e = strided_out<float>(x, y, M, N, K, out_dtype, stream); break;
+    case DSLPG_F16: e = strided_out<__half>(x, y, M, N, K, out_dtype, stream); break;
+    default: e = strided_out<__nv_bfloat16>(x, y, M, N, K, out_dtype, stream); break;
+  }
+  return static_cast<int>(e);
+}

@@ -1,0 +1,42 @@
+"""CUDA (sm_100a) backend of ViperBench ``layer_norm``.
+
+Same signature and error behaviour as ViperBench/layer_norm/pytorch_impl.py:5-12:
+``layer_norm(x, weight, bias, eps=1e-5)`` normalises over ``weight.shape`` (the
+trailing dims of x) and raises ``ValueError`` for any eps other than 1e-5.
+Computes in fp32 and returns a new tensor of x's shape and dtype.
+"""
+import math
+
+import torch
+
+from .. import _lib
+
+
+def layer_norm(x, weight, bias, eps=1e-5):
+    if eps != 1e-5:
+        raise ValueError(f"Only eps=1e-5 is supported (got {eps}). "
+                         "The Triton kernel hardcodes eps=1e-5.")
+    dev = _lib.require_cuda(x, weight, bias, what="layer_norm")
+    xc = _lib.float_code(x, "layer_norm")
+    wc = _lib.float_code(weight, "layer_norm weight")
+    if bias is not None and bias.dtype != weight.dtype:
+        raise TypeError(f"layer_norm: bias dtype {bias.dtype} differs from weight dtype {weight.dtype}")
+    nshape = tuple(weight.shape)
+    if len(nshape) == 0 or tuple(x.shape[x.dim() - len(nshape):]) != nshape or x.dim() < len(nshape):
+        raise ValueError(f"layer_norm: weight shape {nshape} does not match the trailing dims of x {tuple(x.shape)}")
+    if bias is not None and tuple(bias.shape) != nshape:
+        raise ValueError(f"layer_norm: bias shape {tuple(bias.shape)} != weight shape {nshape}")
+    n = math.prod(nshape)
+    m = x.numel() // n if n else 0
+    x = x.contiguous()
+    w = weight.contiguous()
+    b = bias.contiguous() if bias is not None else None
+    y = torch.empty_like(x)
+    if x.numel() == 0:
+        return y
+    with torch.cuda.device(dev):
+        rc = _lib.load().dslpg_layer_norm_fwd(
+            x.data_ptr(), w.data_ptr(), b.data_ptr() if b is not None else None, y.data_ptr(),
+            m, n, xc, wc, float(eps), _lib.stream_handle(dev))
+    _lib.check(rc, "dslpg_layer_norm_fwd")
+    return y

@@ -1,0 +1,23 @@
+"""CUDA (sm_100a) backend of ViperBench ``softmax``.
+
+Same signature as ViperBench/softmax/pytorch_impl.py:4-6: ``softmax(x)`` along
+the last dimension of a tensor of any rank, returning x's dtype.
+"""
+import torch
+
+from .. import _lib
+
+
+def softmax(x):
+    dev = _lib.require_cuda(x, what="softmax")
+    code = _lib.float_code(x, "softmax")
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    if x.numel() == 0:
+        return y
+    n = x.shape[-1] if x.dim() > 0 else 1
+    m = x.numel() // n
+    with torch.cuda.device(dev):
+        rc = _lib.load().dslpg_softmax_fwd(x.data_ptr(), y.data_ptr(), m, n, code, _lib.stream_handle(dev))
+    _lib.check(rc, "dslpg_softmax_fwd")
+    return y

@@ -1,0 +1,136 @@
+/*
+ * dslpg_b200.h — C ABI of the B200 (sm_100a) row-wise reduction backend.
+ *
+ * One entry point per ViperBench kernel of the row-reduction family. Each takes
+ * plain device pointers, sizes and a dtype code, launches on the given stream
+ * and returns 0 on success, a positive cudaError_t when a CUDA call failed, or
+ * a negative DSLPG_ERR_* code when the arguments were rejected before any
+ * launch. No entry point allocates memory, synchronises, or keeps state other
+ * than a per-device cache of SM counts and occupancy figures.
+ *
+ * Layout: every row-wise operand is a dense row-major [M, N] matrix (the
+ * reference flattens x[..., D] to [M, D] the same way). The caller owns every
+ * buffer; inputs are never written.
+ *
+ * Reference interfaces (paths inside tingxi-li/DSLPerfGap):
+ *   layer_norm      ViperBench/layer_norm/pytorch_impl.py:5-12
+ *   rms_norm        ViperBench/rms_norm/pytorch_impl.py:3-10
+ *   softmax         ViperBench/softmax/pytorch_impl.py:4-6
+ *   log_softmax     ViperBench/log_softmax/pytorch_impl.py:4-8
+ *   logsumexp       ViperBench/logsumexp/pytorch_impl.py:3-5
+ *   cross_entropy   ViperBench/cross_entropy/pytorch_impl.py:4-90 and the
+ *                   kernel layout of ViperBench/cross_entropy/triton_impl.py:13-75,123-140
+ */
+#ifndef DSLPG_B200_H
+#define DSLPG_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#define DSLPG_API __attribute__((visibility("default")))
+#else
+#define DSLPG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type codes (storage types; arithmetic is always fp32). */
+enum {
+  DSLPG_F32 = 0,
+  DSLPG_F16 = 1,
+  DSLPG_BF16 = 2,
+  DSLPG_I32 = 3, /* labels only */
+  DSLPG_I64 = 4  /* labels only */
+};
+
+/* Argument errors (returned before anything is launched). */
+enum {
+  DSLPG_OK = 0,
+  DSLPG_ERR_NULL_POINTER = -1,
+  DSLPG_ERR_BAD_SHAPE = -2,
+  DSLPG_ERR_BAD_DTYPE = -3,
+  DSLPG_ERR_BAD_EPS = -4,
+  DSLPG_ERR_BAD_ARGUMENT = -5
+};
+
+/* Library version, (major << 16) | minor. */
+DSLPG_API int dslpg_version(void);
+
+/* Human-readable text for a return code (negative: ours; positive: CUDA's). */
+DSLPG_API const char* dslpg_error_string(int code);
+
+/*
+ * LayerNorm forward over the last dimension:
+ *   y = (x - mean) / sqrt(var + eps) * weight + bias      (var biased)
+ * x, y: [M, N] of x_dtype; weight, bias: [N] of w_dtype (bias may be NULL).
+ * Replaces layer_norm(x, weight, bias, eps) of
+ * ViperBench/layer_norm/pytorch_impl.py:5-12 (F.layer_norm). The eps == 1e-5
+ * restriction of that file is enforced by the Python wrapper, not here.
+ */
+DSLPG_API int dslpg_layer_norm_fwd(const void* x, const void* weight, const void* bias, void* y,
+                         int64_t M, int64_t N, int x_dtype, int w_dtype, float eps,
+                         cudaStream_t stream);
+
+/*
+ * RMSNorm forward over the trailing N elements of each row:
+ *   y = (x / sqrt(mean(x^2) + eps) * weight)  computed in fp32, stored as x_dtype
+ * Replaces rms_norm(x, normalized_shape, weight, eps) of
+ * ViperBench/rms_norm/pytorch_impl.py:3-10.
+ */
+DSLPG_API int dslpg_rms_norm_fwd(const void* x, const void* weight, void* y, int64_t M, int64_t N,
+                       int x_dtype, int w_dtype, float eps, cudaStream_t stream);
+
+/*
+ * Softmax along the last dimension: y = exp(x - max) / sum(exp(x - max)).
+ * Replaces softmax(x) of ViperBench/softmax/pytorch_impl.py:4-6.
+ */
+DSLPG_API int dslpg_softmax_fwd(const void* x, void* y, int64_t M, int64_t N, int dtype,
+                      cudaStream_t stream);
+
+/*
+ * Log-softmax over the middle axis of a dense [M, N, K] tensor
+ * (K == 1 is the last-dimension case): y = x - max - log(sum(exp(x - max))).
+ * x is in_dtype, y is out_dtype; when they differ, x is first rounded to
+ * out_dtype, as F.log_softmax(x, dim, dtype=out_dtype) does.
+ * Replaces log_softmax(x, dim, dtype) of ViperBench/log_softmax/pytorch_impl.py:4-8.
+ */
+DSLPG_API int dslpg_log_softmax_fwd(const void* x, void* y, int64_t M, int64_t N, int64_t K,
+                          int in_dtype, int out_dtype, cudaStream_t stream);
+
+/*
+ * logsumexp along the last dimension, with torch.logsumexp's treatment of
+ * infinite maxima (a +inf entry gives +inf, an all -inf row gives -inf):
+ * y[M] of dtype.  Replaces logsumexp(x) of ViperBench/logsumexp/pytorch_impl.py:3-5.
+ */
+DSLPG_API int dslpg_logsumexp_fwd(const void* x, void* y, int64_t M, int64_t N, int dtype,
+                        cudaStream_t stream);
+
+/*
+ * Blockwise cross-entropy forward. For every row r and column block
+ * cb < ceil(n_cols / block_size) it writes, at flat index cb * n_rows + r of
+ * the three fp32 outputs, the block's log-sum-exp of logits * logit_scale, the
+ * loss term and the z-loss term, exactly as
+ * ViperBench/cross_entropy/pytorch_impl.py:4-90 (and the Triton kernel at
+ * ViperBench/cross_entropy/triton_impl.py:13-75) define them. Flat entries at or
+ * beyond ceil(n_cols / block_size) * n_rows are not written. Under split != 0
+ * the z-loss entries are written as 0.
+ * logits: [n_rows, n_cols] rows `logits_row_stride` elements apart;
+ * labels: [n_rows] of labels_dtype (DSLPG_I32 or DSLPG_I64).
+ * Replaces cross_entropy_fwd(...) of ViperBench/cross_entropy/pytorch_impl.py:4-90.
+ */
+DSLPG_API int dslpg_cross_entropy_fwd(const void* logits, const void* labels, float* loss, float* lse,
+                            float* z_loss, int64_t n_rows, int64_t n_cols,
+                            int64_t logits_row_stride, int logits_dtype, int labels_dtype,
+                            float smoothing, float logit_scale, float lse_square_scale,
+                            int64_t ignored_index, float total_classes, int64_t class_start_idx,
+                            int64_t block_size, int has_smoothing, int split,
+                            cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSLPG_B200_H */

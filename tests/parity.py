@@ -1,0 +1,103 @@
+"""Parity rules shared by the tests (the tolerance is written here, once).
+
+* fp32 outputs: |out - ref| <= 1e-5 + 1e-5 * |ref| (atol = rtol = 1e-5).
+* fp16 / bf16 outputs: within 1 ulp of the output dtype at the fp32-computed
+  reference value; normalised outputs (layer_norm, rms_norm) may also pass
+  with |out - ref| <= 2e-2.
+* NaN and +/-inf must appear at exactly the reference's positions.
+The reference's own check (ViperBench/test_utils.py:11-35, loose=True: fp32
+2e-5, fp16 2e-3, bf16 2e-2, atol = rtol) is `reference_allclose`.
+"""
+from __future__ import annotations
+
+import torch
+
+FP32_TOL = 1e-5
+NORM_ATOL_16 = 2e-2
+_P = {torch.float16: (11, -14), torch.bfloat16: (8, -126), torch.float32: (24, -126)}
+_REF_TOL = {torch.float32: 1e-5, torch.float16: 1e-3, torch.bfloat16: 1e-2}
+
+
+def dtype_ulp(ref: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Spacing of `dtype` numbers at |ref| (ref as float64)."""
+    p, emin = _P[dtype]
+    a = ref.double().abs()
+    e = torch.floor(torch.log2(torch.where(a > 0, a, torch.ones_like(a))))
+    e = torch.clamp(e, min=emin)
+    e = torch.where(a > 0, e, torch.full_like(e, emin))
+    return torch.pow(2.0, e - (p - 1))
+
+
+def compare(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, normalised: bool = False,
+            chunk: int = 1 << 24):
+    """Return (ok, message) for the parity rule above (checked in chunks)."""
+    out = out.detach().reshape(-1)
+    ref = ref.detach().reshape(-1)
+    if out.shape != ref.shape:
+        return False, f"shape {tuple(out.shape)} != {tuple(ref.shape)}"
+    worst = 0.0
+    for s in range(0, max(out.numel(), 1), chunk):
+        ok, msg, w = _compare_chunk(out[s:s + chunk].cpu().double(), ref[s:s + chunk].cpu().double(), dtype,
+                                    normalised, s)
+        if not ok:
+            return False, msg
+        worst = max(worst, w)
+    if dtype == torch.float32:
+        return True, f"max|d|={worst:.3g}"
+    return True, f"max ulps={worst:.3f}"
+
+
+def _compare_chunk(out, ref, dtype, normalised, offset):
+    on, rn = torch.isnan(out), torch.isnan(ref)
+    if not torch.equal(on, rn):
+        return False, f"NaN pattern differs ({int(on.sum())} vs {int(rn.sum())} NaNs)", 0.0
+    oi, ri = torch.isinf(out), torch.isinf(ref)
+    if not torch.equal(oi, ri) or not torch.equal(out[oi], ref[ri]):
+        return False, "inf pattern differs", 0.0
+    fin = ~(rn | ri)
+    o, r = out[fin], ref[fin]
+    if o.numel() == 0:
+        return True, "", 0.0
+    d = (o - r).abs()
+    if dtype == torch.float32:
+        bad = d > FP32_TOL + FP32_TOL * r.abs()
+        what = "atol=rtol=1e-5"
+        worst = d.max().item()
+    else:
+        u = dtype_ulp(r, dtype)
+        bound = u * (1 + 1e-9)
+        if normalised:
+            bound = torch.maximum(bound, torch.full_like(bound, NORM_ATOL_16))
+        bad = d > bound
+        what = "1 ulp" + (" or 2e-2" if normalised else "")
+        worst = (d / u).max().item()
+    if bad.any():
+        i = int(torch.nonzero(bad)[0])
+        return False, (f"{int(bad.sum())}/{d.numel()} values outside {what} (chunk at {offset}); first: "
+                       f"out={o[i].item()!r} ref={r[i].item()!r}; max|d|={d.max().item():.3g}"), worst
+    return True, "", worst
+
+
+def reference_allclose(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype) -> bool:
+    """ViperBench/test_utils.py:21-35 with loose=True, NaN positions compared equal."""
+    tol = 2 * _REF_TOL.get(dtype, 1e-5)
+    return bool(torch.allclose(ref.detach().cpu().float(), out.detach().cpu().float(),
+                               atol=tol, rtol=tol, equal_nan=True))
+
+
+def out_dtype(op: str, args, kwargs) -> torch.dtype:
+    if op == "log_softmax" and kwargs.get("dtype"):
+        return getattr(torch, kwargs["dtype"])
+    if op == "cross_entropy":
+        return torch.float32
+    return args[0].dtype
+
+
+NORMALISED = {"layer_norm", "rms_norm"}
+
+
+def resolve_kwargs(op: str, kwargs: dict) -> dict:
+    kw = dict(kwargs)
+    if op == "log_softmax" and "dtype" in kw:
+        kw["dtype"] = getattr(torch, kw["dtype"])
+    return kw

@@ -1,0 +1,72 @@
+"""The C-ABI library: it loads, exports every entry point that
+include/dslpg_b200.h declares, and rejects bad arguments before launching
+anything (these calls return before any CUDA API call, so they run on CPU)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from dslperfgap_b200 import _lib, build
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "dslpg_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"DSLPG_API\s+[\w\s\*]+?\b(dslpg_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_the_family():
+    names = declared_symbols()
+    for op in ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy"]:
+        assert f"dslpg_{op}_fwd" in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
+
+
+def test_python_binding_covers_header():
+    bound = set(_lib.SIGNATURES) | {"dslpg_error_string"}
+    assert set(declared_symbols()) <= bound
+
+
+def test_version(lib):
+    assert lib.dslpg_version() >= 1
+
+
+@pytest.mark.parametrize("code,text", [(-1, "NULL"), (-2, "shape"), (-3, "dtype"), (-4, "eps"), (0, "success")])
+def test_error_strings(lib, code, text):
+    assert text in lib.dslpg_error_string(code).decode()
+
+
+def test_argument_errors_return_before_launch(lib):
+    # null pointers
+    assert lib.dslpg_softmax_fwd(None, None, 4, 4, 0, None) == -1
+    assert lib.dslpg_layer_norm_fwd(8, None, None, 8, 4, 4, 0, 0, 1e-5, None) == -1
+    assert lib.dslpg_cross_entropy_fwd(8, None, 8, 8, 8, 2, 2, 2, 0, 4, 0, 1, 0, -100, 2, 0, 2, 0, 0, None) == -1
+    # dtype codes
+    assert lib.dslpg_softmax_fwd(8, 8, 4, 4, 7, None) == -3
+    assert lib.dslpg_rms_norm_fwd(8, 8, 8, 4, 4, 0, 9, 1e-5, None) == -3
+    assert lib.dslpg_log_softmax_fwd(8, 8, 4, 4, 1, 0, 3, None) == -3
+    assert lib.dslpg_cross_entropy_fwd(8, 8, 8, 8, 8, 2, 2, 2, 0, 0, 0, 1, 0, -100, 2, 0, 2, 0, 0, None) == -3
+    # shapes
+    assert lib.dslpg_softmax_fwd(8, 8, -1, 4, 0, None) == -2
+    assert lib.dslpg_log_softmax_fwd(8, 8, 4, 4, 0, 0, 0, None) == -2
+    assert lib.dslpg_cross_entropy_fwd(8, 8, 8, 8, 8, 2, 4, 2, 0, 4, 0, 1, 0, -100, 2, 0, 2, 0, 0, None) == -2
+    assert lib.dslpg_cross_entropy_fwd(8, 8, 8, 8, 8, 2, 4, 4, 0, 4, 0, 1, 0, -100, 2, 0, 0, 0, 0, None) == -2
+    # eps
+    assert lib.dslpg_layer_norm_fwd(8, 8, None, 8, 4, 4, 0, 0, float("nan"), None) == -4
+    assert lib.dslpg_rms_norm_fwd(8, 8, 8, 4, 4, 0, 0, -1.0, None) == -4
+    # empty problems are a no-op success
+    assert lib.dslpg_softmax_fwd(8, 8, 0, 4, 0, None) == 0
+    assert lib.dslpg_logsumexp_fwd(8, 8, 0, 4, 0, None) == 0

@@ -1,0 +1,61 @@
+"""The benchmark configurations at their full sizes, CUDA vs the CPU oracle
+on the same seeded inputs (the oracle runs on all host cores), plus
+size-independent properties that hold at any size."""
+import pytest
+import torch
+
+import parity
+from oracle import oracle
+import dslperfgap_b200 as B
+from dslperfgap_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+
+def assert_parity(out, ref, dtype, normalised=False):
+    ok, msg = parity.compare(out, ref, dtype, normalised=normalised)
+    assert ok, msg
+
+
+@pytest.mark.parametrize("name", workloads.NAMES)
+def test_full_size_config_matches_oracle(name):
+    wl = workloads.make(name, seed=0)
+    out = wl.cuda_fn(*wl.to("cuda").args, **wl.kwargs)
+    if wl.op == "cross_entropy":
+        ref = oracle.cross_entropy_fwd(*wl.args, **wl.kwargs, valid_only=True)
+    else:
+        ref = getattr(oracle, wl.fn_name)(*wl.args, **wl.kwargs)
+    if wl.op == "cross_entropy":
+        nv = wl.valid_entries
+        for i, (o, r) in enumerate(zip(out, ref)):
+            assert_parity(o.reshape(-1)[:nv], r.reshape(-1)[:nv], torch.float32)
+    else:
+        assert_parity(out, ref, wl.out_dtype, normalised=wl.op in parity.NORMALISED)
+
+
+def test_softmax_rows_sum_to_one_full_size():
+    wl = workloads.make("softmax_fp16", seed=3)
+    y = B.softmax(wl.args[0].cuda()).float()
+    s = y.sum(-1)
+    # each of 4096 outputs is within half an fp16 ulp (<= 2^-12 relative) of its value
+    assert torch.allclose(s, torch.ones_like(s), atol=4096 * 2.0 ** -12 / 64)
+
+
+def test_logsumexp_shift_invariance_full_size():
+    wl = workloads.make("logsumexp_bf16", seed=4)
+    x = wl.args[0].cuda()
+    a = B.logsumexp(x).float()
+    b = B.logsumexp((x.float() + 4.0).to(torch.bfloat16)).float()
+    # x + 4 is exact in bf16 only for some values; compare within 2 bf16 ulps at |lse| ~ 16
+    assert torch.allclose(b - a, torch.full_like(a, 4.0), atol=0.25)
+
+
+def test_cross_entropy_mean_loss_matches_oracle_full_size():
+    wl = workloads.make("cross_entropy_bf16", seed=0)
+    logits, labels = wl.args[0].cuda(), wl.args[1].cuda()
+    loss, lse, _ = B.cross_entropy_fwd(logits, labels, **wl.kwargs)
+    keep = labels != -100
+    mean = loss.view(-1)[: logits.shape[0]][keep].double().mean().item()
+    ref_loss, _, _ = oracle.cross_entropy_fwd(wl.args[0], wl.args[1], **wl.kwargs, valid_only=True)
+    ref_mean = ref_loss.view(-1)[: logits.shape[0]][keep.cpu()].double().mean().item()
+    assert abs(mean - ref_mean) <= 1e-5 * abs(ref_mean)
