@@ -283,6 +283,7 @@ def eager_reference_expression(wl):
 
 # ------------------------------------------------------------------ measurements
 def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler, with_torch=True):
+    """Time `steps` launches of workload `name`'s kernel (and its torch baseline)."""
     cfg = workloads.CONFIGS[name]
     sharded = name == "layer_norm_bf16_sharded"
     rows = workloads.shard_rows(cfg.M, rank, world) if sharded else None
@@ -430,6 +431,11 @@ def main(argv=None):
     ap.add_argument("--headline-only", action="store_true", help="skip the other configurations")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--path", choices=["auto", "resident", "tma", "stream"], default="auto",
+                    help="force one kernel shape (default: the dispatcher's choice)")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only this backend's kernels (no torch baselines, e2e or CPU baseline); "
+                         "used for profiling")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()
@@ -446,26 +452,30 @@ def main(argv=None):
         torch.distributed.init_process_group("nccl", device_id=dev)
     import dslperfgap_b200._lib as L
     L.load()  # fails loudly when the CUDA library is not built
+    L.check(L.load().dslpg_set_kernel_path(L.PATHS[args.path]), "dslpg_set_kernel_path")
 
     peak, peak_kind = measured_peak()
     timer = Timer(dev, world)
     sampler = ClockSampler(local)
     sampler.start()
 
-    head = measure_workload(args.workload, rank, world, dev, timer, args.steps, args.warmup, peak, sampler)
+    with_torch = not args.kernel_only
+    head = measure_workload(args.workload, rank, world, dev, timer, args.steps, args.warmup, peak, sampler,
+                            with_torch)
     kernels = {args.workload: head}
     if not args.headline_only:
         for name in workloads.NAMES:
             if name != args.workload:
                 kernels[name] = measure_workload(name, rank, world, dev, timer, args.steps, args.warmup, peak,
-                                                 sampler)
-    e2e = measure_e2e(HEADLINE, rank, world, dev, timer, max(3, min(args.steps, 20)), args.warmup) \
-        if args.workload == HEADLINE else None
+                                                 sampler, with_torch)
+    e2e_steps = max(3, min(args.steps, 20))
+    e2e = measure_e2e(HEADLINE, rank, world, dev, timer, e2e_steps, args.warmup) \
+        if args.workload == HEADLINE and not args.kernel_only else None
     sampler.stop()
     clocks = sampler.summary()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.kernel_only):
         cpu = run_cpu_baseline(args.workload, args.cpu_seconds)
 
     if world > 1:
@@ -487,7 +497,9 @@ def main(argv=None):
                          if peak_kind == "measured" else "fallback 6.65 TB/s"},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": sum(k["launches"] for k in kernels.values()) + (e2e and max(3, min(args.steps, 20)) or 0),
+            "kernel_path": args.path,
+            "wait_timeouts": L.take_wait_timeouts(),
+            "gpu_launches": sum(k["launches"] for k in kernels.values()) + (e2e_steps if e2e else 0),
             "clocks": clocks,
             "kernels": kernels,
         }

@@ -35,7 +35,10 @@ SIGNATURES = {
         _c_f32, _c_f32, _c_f32, _c_i64, _c_f32, _c_i64, _c_i64, _c_int, _c_int, _vp,
     ],
     "dslpg_version": [],
+    "dslpg_set_kernel_path": [_c_int],
 }
+
+PATHS = {"auto": 0, "resident": 1, "tma": 2, "stream": 3}
 
 _lock = threading.Lock()
 _lib = None
@@ -58,6 +61,8 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
                 fn.restype = ctypes.c_int
+            lib.dslpg_take_wait_timeouts.argtypes = []
+            lib.dslpg_take_wait_timeouts.restype = ctypes.c_uint
             lib.dslpg_error_string.argtypes = [ctypes.c_int]
             lib.dslpg_error_string.restype = ctypes.c_char_p
             _lib = lib
@@ -97,3 +102,25 @@ def require_cuda(*tensors, what: str) -> torch.device:
 
 def stream_handle(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
+
+
+class kernel_path:
+    """Context manager forcing one kernel shape ("auto", "resident", "tma",
+    "stream") for the calls made inside it (process-wide; for tests and
+    benchmarks)."""
+
+    def __init__(self, name: str):
+        self.code = PATHS[name]
+
+    def __enter__(self):
+        check(load().dslpg_set_kernel_path(self.code), "dslpg_set_kernel_path")
+        return self
+
+    def __exit__(self, *exc):
+        load().dslpg_set_kernel_path(0)
+        return False
+
+
+def take_wait_timeouts() -> int:
+    """Device-side pipeline waits that ran out of time since the last call."""
+    return int(load().dslpg_take_wait_timeouts())

@@ -1,4 +1,5 @@
 // capi.cu — library-wide C entry points and the host launch helpers.
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -27,6 +28,16 @@ struct OccKeyHash {
   }
 };
 std::mutex g_occ_mu;
+std::atomic<int> g_path{DSLPG_PATH_AUTO};
+struct SmemKey {
+  int dev;
+  const void* fn;
+  bool operator==(const SmemKey& o) const { return dev == o.dev && fn == o.fn; }
+};
+struct SmemKeyHash {
+  size_t operator()(const SmemKey& k) const { return std::hash<const void*>()(k.fn) ^ static_cast<size_t>(k.dev); }
+};
+std::unordered_map<SmemKey, size_t, SmemKeyHash> g_smem;
 std::unordered_map<OccKey, int, OccKeyHash> g_occ;
 }  // namespace
 
@@ -63,7 +74,37 @@ int persistent_grid(const void* kernel, int block, size_t smem, int64_t work_cta
   return static_cast<int>(work_ctas < full ? work_ctas : full);
 }
 
+cudaError_t allow_dynamic_smem(const void* kernel, size_t bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  auto it = g_smem.find(SmemKey{dev, kernel});
+  if (it != g_smem.end() && it->second >= bytes) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) {
+    g_smem[SmemKey{dev, kernel}] = bytes;
+    // occupancy depends on the attribute: forget cached figures for this kernel
+    for (auto o = g_occ.begin(); o != g_occ.end();) {
+      if (o->first.fn == kernel && o->first.dev == dev) o = g_occ.erase(o);
+      else ++o;
+    }
+  }
+  return e;
+}
+
+int kernel_path() { return g_path.load(std::memory_order_relaxed); }
+
 }  // namespace dslpg
+
+extern "C" int dslpg_set_kernel_path(int path) {
+  if (path < DSLPG_PATH_AUTO || path > DSLPG_PATH_STREAM) return DSLPG_ERR_BAD_ARGUMENT;
+  dslpg::g_path.store(path);
+  return DSLPG_OK;
+}
+
+extern "C" unsigned int dslpg_take_wait_timeouts(void) {
+  return dslpg::take_wait_timeouts_rownorm() + dslpg::take_wait_timeouts_rowstat();
+}
 
 extern "C" int dslpg_version(void) { return (0 << 16) | 1; }
 

@@ -214,6 +214,16 @@ int sm_count();
 // than there is work for. `kernel` is the kernel's host stub.
 int persistent_grid(const void* kernel, int block, size_t smem, int64_t work_ctas);
 
+// Allow `kernel` to use `bytes` of dynamic shared memory (cached per device).
+cudaError_t allow_dynamic_smem(const void* kernel, size_t bytes);
+
+// Kernel-shape override (DSLPG_PATH_*), set by dslpg_set_kernel_path.
+int kernel_path();
+
+// Per-file counters of bounded waits that ran out of time (read and reset).
+unsigned int take_wait_timeouts_rownorm();
+unsigned int take_wait_timeouts_rowstat();
+
 inline int dtype_size(int dt) { return dt == DSLPG_F32 ? 4 : 2; }
 inline bool is_float_dtype(int dt) { return dt == DSLPG_F32 || dt == DSLPG_F16 || dt == DSLPG_BF16; }
 inline bool aligned(const void* p, int bytes) {

@@ -23,6 +23,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "pipe.cuh"
 
 namespace dslpg {
 
@@ -66,15 +67,165 @@ DSLPG_DEV void load_weight(const void* p, int j, float* out) {
 }
 
 // ============================================================================
-// Resident kernel
+// Per-row math shared by the resident and TMA kernels
+// ============================================================================
+// Normalise one row whose VPT 16-byte vectors (elements [j*E, j*E+E) with
+// j = t + k*tpr) this thread holds in v; masked vectors hold zeros. Stores the
+// thread's part of the output row yr. Every thread of the row group calls it.
+template <int OP, typename Tin, typename Tout, int VPT, int CACHE_LIMIT, class Red>
+DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool (&ok)[VPT], int t,
+                             Tout* yr, Red& rd) {
+  constexpr int E = Elt<Tin>::kPerVec;
+  // Up to CACHE_LIMIT fp32 values per thread are kept unpacked (softmax keeps
+  // the exp values there, so each element costs one ex2); longer slices stay
+  // packed and are unpacked again in each phase.
+  constexpr bool kCache = VPT * E <= CACHE_LIMIT;
+  const float n_f = static_cast<float>(a.N);
+
+  float fr[kCache ? VPT : 1][E];
+  if constexpr (kCache) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      unpack<Tin>(v[k], fr[k]);
+#pragma unroll
+      for (int i = 0; i < E; ++i) fr[k][i] = in_value<Tin, Tout>(fr[k][i]);
+    }
+  }
+  // The fp32 values of vector k (masked vectors read as 0).
+  auto get = [&](int k, float* f) {
+    if constexpr (kCache) {
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] = fr[k][i];
+    } else {
+      unpack<Tin>(v[k], f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
+    }
+  };
+
+  if constexpr (OP == kRmsNorm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      float f[E];
+      get(k, f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) ss = fmaf(f[i], f[i], ss);
+    }
+    ss = rd.template reduce<SumOp>(ss);
+    const float inv = 1.0f / sqrtf(ss / n_f + a.eps);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!ok[k]) continue;
+      const int j = t + k * a.tpr;
+      float f[E], w[E];
+      get(k, f);
+      load_weight<Tin, E>(a.w, j, w);
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] = (f[i] * inv) * w[i];
+      StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+    }
+  } else if constexpr (OP == kLayerNorm) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      float f[E];
+      get(k, f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) s += f[i];
+    }
+    s = rd.template reduce<SumOp>(s);
+    const float mean = s / n_f;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!ok[k]) continue;
+      float f[E];
+      get(k, f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const float d = f[i] - mean;
+        q = fmaf(d, d, q);
+      }
+    }
+    q = rd.template reduce<SumOp>(q);
+    const float rstd = 1.0f / sqrtf(q / n_f + a.eps);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!ok[k]) continue;
+      const int j = t + k * a.tpr;
+      float f[E], w[E], bb[E];
+      get(k, f);
+      load_weight<Tin, E>(a.w, j, w);
+      load_weight<Tin, E>(a.b, j, bb);
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - mean) * rstd, w[i], bb[i]);
+      StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+    }
+  } else {  // kSoftmax / kLogSoftmax
+    float m = kNegInf;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!ok[k]) continue;
+      float f[E];
+      get(k, f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) m = max_nan(m, f[i]);
+    }
+    m = rd.template reduce<MaxOp>(m);
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!ok[k]) continue;
+      float f[E];
+      get(k, f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const float e = exp_shifted(f[i] - m);
+        if constexpr (kCache && OP == kSoftmax) fr[k][i] = e;
+        s += e;
+      }
+    }
+    s = rd.template reduce<SumOp>(s);
+    if constexpr (OP == kSoftmax) {
+      const float inv = 1.0f / s;
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        const int j = t + k * a.tpr;
+        float f[E];
+        if constexpr (kCache) {
+#pragma unroll
+          for (int i = 0; i < E; ++i) f[i] = fr[k][i] * inv;
+        } else {
+          get(k, f);
+#pragma unroll
+          for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - m) * inv;
+        }
+        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+      }
+    } else {
+      const float ls = logf(s);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        const int j = t + k * a.tpr;
+        float f[E];
+        get(k, f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = (f[i] - m) - ls;
+        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+      }
+    }
+  }
+}
+
+// ============================================================================
+// Resident kernel: rows read straight into registers
 // ============================================================================
 template <int OP, typename Tin, typename Tout, int VPT>
 __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
   constexpr int E = Elt<Tin>::kPerVec;
-  // Up to 16 fp32 values per thread are kept unpacked (softmax keeps the exp
-  // values there, so each element costs one ex2); longer slices stay packed and
-  // are unpacked again in each phase.
-  constexpr bool kCache = VPT * E <= 16;
   // With <= 4 vectors per thread the next row's vectors are loaded before this
   // row is reduced, so every thread always has loads in flight.
   constexpr bool kPrefetch = VPT <= 4;
@@ -82,10 +233,7 @@ __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
 
   const int g = threadIdx.x / a.tpr;
   const int t = threadIdx.x - g * a.tpr;
-  const int nw = a.tpr >> 5;
-  const int first_warp = g * nw;
-  const float n_f = static_cast<float>(a.N);
-  int buf = 0;
+  GroupReducer rd{red, a.tpr >> 5, g * (a.tpr >> 5), 0};
 
   auto load_row = [&](Vec16* dst, int64_t row) {
 #pragma unroll
@@ -103,8 +251,6 @@ __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
 
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * a.rpc; base < a.M; base += step) {
     const int64_t row = base + g;
-    Tout* yr = static_cast<Tout*>(a.y) + row * a.N;
-
     Vec16 v[VPT];
     if constexpr (kPrefetch) {
 #pragma unroll
@@ -116,148 +262,82 @@ __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
     bool ok[VPT];
 #pragma unroll
     for (int k = 0; k < VPT; ++k) ok[k] = row < a.M && (t + k * a.tpr) < a.nvec;
+    // 16 cached values: the prefetch buffer needs the other registers.
+    normalize_row<OP, Tin, Tout, VPT, 16>(a, v, ok, t, static_cast<Tout*>(a.y) + row * a.N, rd);
+  }
+}
 
-    float fr[kCache ? VPT : 1][E];
-    if constexpr (kCache) {
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        unpack<Tin>(v[k], fr[k]);
-#pragma unroll
-        for (int i = 0; i < E; ++i) fr[k][i] = in_value<Tin, Tout>(fr[k][i]);
-      }
-    }
-    // The fp32 values of vector k (masked vectors read as 0).
-    auto get = [&](int k, float* f) {
-      if constexpr (kCache) {
-#pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = fr[k][i];
-      } else {
-        unpack<Tin>(v[k], f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
-      }
-    };
+// ============================================================================
+// TMA kernel: rows streamed into a shared-memory ring by bulk copies
+// ============================================================================
+// Counts waits that ran out of time in this file's kernels (read and reset
+// by dslpg_take_wait_timeouts).
+static __device__ unsigned int g_wait_timeouts;
 
-    if constexpr (OP == kRmsNorm) {
-      float ss = 0.f;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        float f[E];
-        get(k, f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) ss = fmaf(f[i], f[i], ss);
-      }
-      ss = group_reduce<SumOp>(ss, red[buf], nw, first_warp);
-      buf ^= 1;
-      const float inv = 1.0f / sqrtf(ss / n_f + a.eps);
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        if (!ok[k]) continue;
-        const int j = t + k * a.tpr;
-        float f[E], w[E];
-        get(k, f);
-        load_weight<Tin, E>(a.w, j, w);
-#pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = (f[i] * inv) * w[i];
-        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
-      }
-    } else if constexpr (OP == kLayerNorm) {
-      float s = 0.f;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        float f[E];
-        get(k, f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) s += f[i];
-      }
-      s = group_reduce<SumOp>(s, red[buf], nw, first_warp);
-      buf ^= 1;
-      const float mean = s / n_f;
-      float q = 0.f;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        if (!ok[k]) continue;
-        float f[E];
-        get(k, f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const float d = f[i] - mean;
-          q = fmaf(d, d, q);
+// Warp 0 lane 0 is the producer: it copies each of the CTA's rows (rows
+// blockIdx.x, blockIdx.x + gridDim.x, ...) into the next ring slot. Warps 1..
+// are the a.tpr consumers: each waits for the row, copies its VPT vectors to
+// registers, releases the slot, and normalises the row with stores straight
+// from registers. A wait that runs out of time sets `abort`: every thread then
+// still runs the same loop (so the consumers' named barriers stay matched) but
+// skips the remaining waits; the producer stops issuing and drains.
+template <int OP, typename Tin, typename Tout, int VPT>
+__global__ void __launch_bounds__(1024) tma_norm_kernel(const RowArgs a, int stages,
+                                                        unsigned long long limit_ns) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int E = Elt<Tin>::kPerVec;
+  __shared__ volatile int abort_flag;
+  const int ncw = (blockDim.x >> 5) - 1;
+  const uint32_t row_bytes = static_cast<uint32_t>(a.N) * sizeof(Tin);
+  if (threadIdx.x == 0) abort_flag = 0;
+  float* red;
+  const Ring ring = ring_setup(smem, row_bytes, stages, ncw, &red);  // includes __syncthreads
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      uint32_t u = 0;
+      for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x, ++u) {
+        if (abort_flag) break;
+        if (u >= static_cast<uint32_t>(stages) && !mbar_wait(ring.empty_bar(u), ring.parity(u) ^ 1u, limit_ns)) {
+          atomicAdd(&g_wait_timeouts, 1u);
+          abort_flag = 1;
+          break;
         }
+        mbar_arrive_expect_tx(ring.full_bar(u), row_bytes);
+        bulk_load(ring.slot(u), static_cast<const Tin*>(a.x) + row * a.N, row_bytes, ring.full_bar(u), pol);
       }
-      q = group_reduce<SumOp>(q, red[buf], nw, first_warp);
-      buf ^= 1;
-      const float rstd = 1.0f / sqrtf(q / n_f + a.eps);
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        if (!ok[k]) continue;
-        const int j = t + k * a.tpr;
-        float f[E], w[E], bb[E];
-        get(k, f);
-        load_weight<Tin, E>(a.w, j, w);
-        load_weight<Tin, E>(a.b, j, bb);
-#pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - mean) * rstd, w[i], bb[i]);
-        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
-      }
-    } else {  // kSoftmax / kLogSoftmax
-      float m = kNegInf;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        if (!ok[k]) continue;
-        float f[E];
-        get(k, f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) m = max_nan(m, f[i]);
-      }
-      m = group_reduce<MaxOp>(m, red[buf], nw, first_warp);
-      buf ^= 1;
-      float s = 0.f;
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        if (!ok[k]) continue;
-        float f[E];
-        get(k, f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const float e = exp_shifted(f[i] - m);
-          if constexpr (kCache && OP == kSoftmax) fr[k][i] = e;
-          s += e;
-        }
-      }
-      s = group_reduce<SumOp>(s, red[buf], nw, first_warp);
-      buf ^= 1;
-      if constexpr (OP == kSoftmax) {
-        const float inv = 1.0f / s;
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          if (!ok[k]) continue;
-          const int j = t + k * a.tpr;
-          float f[E];
-          if constexpr (kCache) {
-#pragma unroll
-            for (int i = 0; i < E; ++i) f[i] = fr[k][i] * inv;
-          } else {
-            get(k, f);
-#pragma unroll
-            for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - m) * inv;
-          }
-          StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
-        }
-      } else {
-        const float ls = logf(s);
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          if (!ok[k]) continue;
-          const int j = t + k * a.tpr;
-          float f[E];
-          get(k, f);
-#pragma unroll
-          for (int i = 0; i < E; ++i) f[i] = (f[i] - m) - ls;
-          StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
-        }
-      }
+      if (!ring_drain(ring, u)) atomicAdd(&g_wait_timeouts, 1u);
     }
+    return;
+  }
+
+  const int t = threadIdx.x - 32;
+  ConsumerReducer rd{red, ncw, 0};
+  uint32_t u = 0;
+  for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x, ++u) {
+    if (!abort_flag && !mbar_wait(ring.full_bar(u), ring.parity(u), limit_ns)) {
+      atomicAdd(&g_wait_timeouts, 1u);
+      abort_flag = 1;
+    }
+    Vec16 v[VPT];
+    bool ok[VPT];
+    const uint32_t slot = ring.slot(u);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int j = t + k * a.tpr;
+      ok[k] = j < a.nvec;
+      v[k] = Vec16{{0u, 0u, 0u, 0u}};
+      if (ok[k]) v[k] = lds16(slot + 16u * j);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(ring.empty_bar(u));
+    if (abort_flag) {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) ok[k] = false;  // no stores after a timeout
+    }
+    normalize_row<OP, Tin, Tout, VPT, 32>(a, v, ok, t, static_cast<Tout*>(a.y) + row * a.N, rd);
   }
 }
 
@@ -549,16 +629,51 @@ cudaError_t launch_stream(RowArgs a, cudaStream_t st) {
 // per thread over 1024 threads) or 64 KiB of 16-bit data (4 vectors per thread;
 // 8 packed 16-bit vectors per thread do not fit the 64-register budget).
 
+// Shared memory given to a TMA CTA's ring (a few CTAs fit on one SM).
+constexpr uint32_t kTmaRingBytes = 64u * 1024u;
+// Rows handled by the TMA kernel: [kTmaMinRow, kTmaMaxRow] bytes.
+constexpr uint32_t kTmaMinRow = 2048u, kTmaMaxRow = 32768u;
+
+template <int OP, typename Tin, typename Tout, int VPT>
+cudaError_t launch_tma(RowArgs a, cudaStream_t st) {
+  a.tpr = round_up32((a.nvec + VPT - 1) / VPT);
+  a.rpc = 1;
+  const int block = a.tpr + 32;
+  const uint32_t row_bytes = static_cast<uint32_t>(a.N) * sizeof(Tin);
+  uint32_t stages = kTmaRingBytes / row_bytes;
+  stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
+  const size_t smem = RingLayout::total_bytes(row_bytes, static_cast<int>(stages));
+  const void* fn = reinterpret_cast<const void*>(&tma_norm_kernel<OP, Tin, Tout, VPT>);
+  if (cudaError_t e = allow_dynamic_smem(fn, smem)) return e;
+  const int grid = persistent_grid(fn, block, smem, a.M);
+  tma_norm_kernel<OP, Tin, Tout, VPT><<<grid, block, smem, st>>>(a, static_cast<int>(stages), kWaitLimitNs);
+  return cudaGetLastError();
+}
+
 template <int OP, typename Tin, typename Tout>
 cudaError_t dispatch_rows(RowArgs a, cudaStream_t st) {
   constexpr int E = Elt<Tin>::kPerVec;
+  const int path = kernel_path();
   const bool vec = (a.N % E == 0) && aligned(a.x, 16) &&
                    aligned(a.y, E * static_cast<int>(sizeof(Tout)));
-  if (vec) {
+  const bool weights_ok = (OP != kLayerNorm && OP != kRmsNorm) || a.wvec;
+  if (vec && weights_ok && path != DSLPG_PATH_STREAM) {
     a.nvec = a.N / E;
-    const bool weights_ok = (OP != kLayerNorm && OP != kRmsNorm) || a.wvec;
+    const uint32_t row_bytes = static_cast<uint32_t>(a.N) * sizeof(Tin);
+    const bool tma_fits = row_bytes >= kTmaMinRow && row_bytes <= kTmaMaxRow;
+    if ((path == DSLPG_PATH_AUTO && tma_fits) || (path == DSLPG_PATH_TMA && row_bytes <= kTmaMaxRow)) {
+      // 32 elements per thread; fewer when the row is short.
+      constexpr int kV = 32 / E;
+      if (a.nvec >= 32 * kV) return launch_tma<OP, Tin, Tout, kV>(a, st);
+      if (a.nvec > 32) return launch_tma<OP, Tin, Tout, 2>(a, st);
+      return launch_tma<OP, Tin, Tout, 1>(a, st);
+    }
+    // Largest row (in 16-byte vectors) kept in registers: 128 KiB of fp32 (8
+    // vectors per thread over 1024 threads) or 64 KiB of 16-bit data (4 vectors
+    // per thread; 8 packed 16-bit vectors per thread do not fit the
+    // 64-register budget).
     const int max_resident = (E == 4) ? 8192 : 4096;
-    if (a.nvec <= max_resident && weights_ok) {
+    if (a.nvec <= max_resident && path != DSLPG_PATH_TMA) {
       // About 16 elements per thread (4 fp32 or 2 16-bit vectors), more only
       // when the row would need more than 1024 threads, fewer for short rows.
       constexpr int kBase = (E == 4) ? 4 : 2;
@@ -570,6 +685,10 @@ cudaError_t dispatch_rows(RowArgs a, cudaStream_t st) {
       if (a.nvec > 32) return launch_resident<OP, Tin, Tout, 2>(a, st);
       return launch_resident<OP, Tin, Tout, 1>(a, st);
     }
+    if (vec) return launch_stream<OP, Tin, Tout, E>(a, st);
+  }
+  if (vec) {
+    a.nvec = a.N / E;
     return launch_stream<OP, Tin, Tout, E>(a, st);
   }
   a.nvec = 0;
@@ -704,3 +823,12 @@ extern "C" int dslpg_log_softmax_fwd(const void* x, void* y, int64_t M, int64_t 
   }
   return static_cast<int>(e);
 }
+
+namespace dslpg {
+unsigned int take_wait_timeouts_rownorm() {
+  unsigned int v = 0, zero = 0;
+  cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
+  cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero));
+  return v;
+}
+}  // namespace dslpg

@@ -15,6 +15,7 @@
 // index cb * n_rows + r, the layout of
 // ViperBench/cross_entropy/triton_impl.py:46,75-76.
 #include "common.cuh"
+#include "pipe.cuh"
 
 namespace dslpg {
 
@@ -57,6 +58,49 @@ DSLPG_DEV void fold_chunk(float& m, float& s, const float* t) {
   for (int i = 0; i < n; ++i) acc += ex2(t[i] - nm);
   s = acc;
   m = nm;
+}
+
+// Write the results of work item (row r, block cb) from the merged online
+// statistics: gm = max of t, gs = sum of 2^(t - gm), gsum = sum of x (SMOOTH).
+template <int KIND, typename T, bool SMOOTH>
+DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col0, float gm, float gs,
+                           float gsum) {
+  const float lse_fin = (gm + log2f(gs)) * kLn2;
+  if constexpr (KIND == kLse) {
+    // torch.logsumexp shifts by the max only when it is finite.
+    float v = lse_fin;
+    if (gm == kPosInf) v = kPosInf;
+    else if (gm == kNegInf) v = kNegInf;
+    static_cast<T*>(a.out)[r] = from_f<T>(v);
+  } else {
+    const float lse = (fabsf(gm) < kPosInf) ? lse_fin : kNaN;
+    const int64_t oi = cb * a.M + r;
+    a.lse[oi] = lse;
+    const int64_t label = a.label64 ? static_cast<const int64_t*>(a.labels)[r]
+                                    : static_cast<int64_t>(static_cast<const int32_t*>(a.labels)[r]);
+    float loss = 0.f, z = 0.f;
+    if (label != a.ignored) {
+      const int64_t adj = label - a.class_start;
+      const float lse_term = a.split ? 0.f : lse;
+      const float sum_logits = gsum * a.scale;
+      const int64_t hi = (cb + 1) * a.seg < a.N ? (cb + 1) * a.seg : a.N;
+      if (adj >= col0 && adj < hi) {
+        const float xl = to_f(static_cast<const T*>(a.x)[r * a.ld + adj]) * a.scale;
+        if constexpr (SMOOTH)
+          loss = lse_term - a.smoothing * sum_logits / a.total_classes - (1.f - a.smoothing) * xl;
+        else
+          loss = lse_term - xl;
+      } else if constexpr (SMOOTH) {
+        loss = a.smoothing * (lse_term - sum_logits / a.total_classes);
+      }
+      if (!a.split) {
+        z = a.lse_sq * lse * lse;
+        loss += z;
+      }
+    }
+    a.loss[oi] = loss;
+    a.zloss[oi] = z;
+  }
 }
 
 template <int KIND, typename T, int V, bool SMOOTH>
@@ -134,44 +178,109 @@ __global__ void __launch_bounds__(1024) rowstat_kernel(const StatArgs a) {
       buf ^= 1;
     }
 
-    if (t == 0 && iv) {
-      const float lse_fin = (gm + log2f(gs)) * kLn2;
-      if constexpr (KIND == kLse) {
-        // torch.logsumexp shifts by the max only when it is finite.
-        float v = lse_fin;
-        if (gm == kPosInf) v = kPosInf;
-        else if (gm == kNegInf) v = kNegInf;
-        static_cast<T*>(a.out)[r] = from_f<T>(v);
-      } else {
-        const float lse = (fabsf(gm) < kPosInf) ? lse_fin : kNaN;
-        const int64_t oi = cb * a.M + r;
-        a.lse[oi] = lse;
-        const int64_t label = a.label64 ? static_cast<const int64_t*>(a.labels)[r]
-                                        : static_cast<int64_t>(static_cast<const int32_t*>(a.labels)[r]);
-        float loss = 0.f, z = 0.f;
-        if (label != a.ignored) {
-          const int64_t adj = label - a.class_start;
-          const float lse_term = a.split ? 0.f : lse;
-          const float sum_logits = gsum * a.scale;
-          const int64_t hi = (cb + 1) * a.seg < a.N ? (cb + 1) * a.seg : a.N;
-          if (adj >= col0 && adj < hi) {
-            const float xl = to_f(static_cast<const T*>(a.x)[r * a.ld + adj]) * a.scale;
-            if constexpr (SMOOTH)
-              loss = lse_term - a.smoothing * sum_logits / a.total_classes - (1.f - a.smoothing) * xl;
-            else
-              loss = lse_term - xl;
-          } else if constexpr (SMOOTH) {
-            loss = a.smoothing * (lse_term - sum_logits / a.total_classes);
+    if (t == 0 && iv) finish_item<KIND, T, SMOOTH>(a, r, cb, col0, gm, gs, gsum);
+  }
+}
+
+// Counts waits that ran out of time in this file's kernels.
+static __device__ unsigned int g_wait_timeouts;
+
+// TMA-pipelined variant for long work items (vocab-sized rows): warp 0 lane 0
+// streams each item of the CTA (items blockIdx.x, blockIdx.x + gridDim.x, ...)
+// in chunks of up to chunk_bytes into the shared-memory ring; the consumer
+// warps fold every chunk into per-thread online statistics (VPC vectors per
+// thread per chunk), release the slot, and merge per item. Timeouts are
+// handled as in the normalising TMA kernel: the loop shape never changes, so
+// the consumers' named barriers stay matched.
+template <int KIND, typename T, bool SMOOTH>
+__global__ void __launch_bounds__(1024) tma_stat_kernel(const StatArgs a, int stages, uint32_t chunk_bytes,
+                                                        unsigned long long limit_ns) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int E = Elt<T>::kPerVec;
+  constexpr int VPC = 4;
+  __shared__ volatile int abort_flag;
+  const int ncw = (blockDim.x >> 5) - 1;
+  const int C = ncw * 32;
+  if (threadIdx.x == 0) abort_flag = 0;
+  float* red;
+  const Ring ring = ring_setup(smem, chunk_bytes, stages, ncw, &red);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t items = a.M * a.nseg;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      uint32_t u = 0;
+      bool stop = false;
+      for (int64_t item = blockIdx.x; item < items && !stop; item += gridDim.x) {
+        const int64_t r = item / a.nseg, cb = item - r * a.nseg;
+        const int64_t col0 = cb * a.seg;
+        const int64_t len = (a.N - col0) < a.seg ? (a.N - col0) : a.seg;
+        const char* src = reinterpret_cast<const char*>(static_cast<const T*>(a.x) + r * a.ld + col0);
+        const uint32_t bytes = static_cast<uint32_t>(len * sizeof(T));
+        for (uint32_t off = 0; off < bytes; off += chunk_bytes, ++u) {
+          if (abort_flag) { stop = true; break; }
+          if (u >= static_cast<uint32_t>(stages) && !mbar_wait(ring.empty_bar(u), ring.parity(u) ^ 1u, limit_ns)) {
+            atomicAdd(&g_wait_timeouts, 1u);
+            abort_flag = 1;
+            stop = true;
+            break;
           }
-          if (!a.split) {
-            z = a.lse_sq * lse * lse;
-            loss += z;
-          }
+          const uint32_t n = (bytes - off) < chunk_bytes ? (bytes - off) : chunk_bytes;
+          mbar_arrive_expect_tx(ring.full_bar(u), n);
+          bulk_load(ring.slot(u), src + off, n, ring.full_bar(u), pol);
         }
-        a.loss[oi] = loss;
-        a.zloss[oi] = z;
       }
+      if (!ring_drain(ring, u)) atomicAdd(&g_wait_timeouts, 1u);
     }
+    return;
+  }
+
+  const int t = threadIdx.x - 32;
+  ConsumerReducer rd{red, ncw, 0};
+  uint32_t u = 0;
+  for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+    const int64_t r = item / a.nseg, cb = item - r * a.nseg;
+    const int64_t col0 = cb * a.seg;
+    const int64_t len = (a.N - col0) < a.seg ? (a.N - col0) : a.seg;
+    const uint32_t bytes = static_cast<uint32_t>(len * sizeof(T));
+    float m = kNegInf, s = 0.f, sum = 0.f;
+    for (uint32_t off = 0; off < bytes; off += chunk_bytes, ++u) {
+      if (!abort_flag && !mbar_wait(ring.full_bar(u), ring.parity(u), limit_ns)) {
+        atomicAdd(&g_wait_timeouts, 1u);
+        abort_flag = 1;
+      }
+      const uint32_t nv = ((bytes - off) < chunk_bytes ? (bytes - off) : chunk_bytes) / 16u;
+      const uint32_t slot = ring.slot(u);
+      Vec16 v[VPC];
+#pragma unroll
+      for (int k = 0; k < VPC; ++k) {
+        const uint32_t j = t + k * C;
+        v[k] = Vec16{{0u, 0u, 0u, 0u}};
+        if (j < nv) v[k] = lds16(slot + 16u * j);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ring.empty_bar(u));
+      float tv[VPC * E];
+#pragma unroll
+      for (int k = 0; k < VPC; ++k) {
+        const bool ok = static_cast<uint32_t>(t + k * C) < nv;
+        float f[E];
+        unpack<T>(v[k], f);
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          if constexpr (SMOOTH) sum += f[i];  // masked vectors read as 0
+          tv[k * E + i] = ok ? f[i] * a.c : kNegInf;
+        }
+      }
+      fold_chunk<VPC * E>(m, s, tv);
+    }
+    const float gm = rd.template reduce<MaxOp>(m);
+    const float sc = (m == gm) ? s : s * ex2(m - gm);
+    const float gs = rd.template reduce<SumOp>(sc);
+    float gsum = 0.f;
+    if constexpr (SMOOTH) gsum = rd.template reduce<SumOp>(sum);
+    if (t == 0 && !abort_flag) finish_item<KIND, T, SMOOTH>(a, r, cb, col0, gm, gs, gsum);
   }
 }
 
@@ -197,11 +306,38 @@ cudaError_t launch_stat(StatArgs a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// TMA path: work items of at least kTmaMinItem bytes, streamed in chunks of
+// kTmaChunk bytes through a ring of kTmaStages slots (two CTAs per SM).
+constexpr uint32_t kTmaChunk = 16u * 1024u;
+constexpr int kTmaStages = 6;
+constexpr int64_t kTmaMinItem = 32 * 1024;
+constexpr int kTmaConsumers = 256;
+
+template <int KIND, typename T, bool SMOOTH>
+cudaError_t launch_tma_stat(StatArgs a, cudaStream_t st) {
+  a.tpr = kTmaConsumers;
+  a.rpc = 1;
+  const int block = kTmaConsumers + 32;
+  const size_t smem = RingLayout::total_bytes(kTmaChunk, kTmaStages);
+  const void* fn = reinterpret_cast<const void*>(&tma_stat_kernel<KIND, T, SMOOTH>);
+  if (cudaError_t e = allow_dynamic_smem(fn, smem)) return e;
+  const int grid = persistent_grid(fn, block, smem, a.M * a.nseg);
+  tma_stat_kernel<KIND, T, SMOOTH><<<grid, block, smem, st>>>(a, kTmaStages, kTmaChunk, kWaitLimitNs);
+  return cudaGetLastError();
+}
+
 template <int KIND, typename T, bool SMOOTH>
 cudaError_t dispatch_vec(StatArgs a, cudaStream_t st) {
   constexpr int E = Elt<T>::kPerVec;
+  const int path = kernel_path();
   const bool vec = aligned(a.x, 16) && (a.ld % E == 0) && (a.seg % E == 0);
-  if (vec) return launch_stat<KIND, T, E, SMOOTH>(a, st);
+  // every item's byte count must be a multiple of 16 for the bulk copies
+  const bool tma_ok = vec && (a.N % E == 0);
+  const int64_t item_bytes = a.seg * static_cast<int64_t>(sizeof(T));
+  if (tma_ok && path != DSLPG_PATH_RESIDENT && path != DSLPG_PATH_STREAM &&
+      (item_bytes >= kTmaMinItem || path == DSLPG_PATH_TMA))
+    return launch_tma_stat<KIND, T, SMOOTH>(a, st);
+  if (vec && path != DSLPG_PATH_STREAM) return launch_stat<KIND, T, E, SMOOTH>(a, st);
   return launch_stat<KIND, T, 1, SMOOTH>(a, st);
 }
 
@@ -277,3 +413,12 @@ extern "C" int dslpg_cross_entropy_fwd(const void* logits, const void* labels, f
                                 : dispatch_dtype<kXent, false>(a, logits_dtype, stream);
   return static_cast<int>(e);
 }
+
+namespace dslpg {
+unsigned int take_wait_timeouts_rowstat() {
+  unsigned int v = 0, zero = 0;
+  cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
+  cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero));
+  return v;
+}
+}  // namespace dslpg

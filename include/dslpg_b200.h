@@ -56,6 +56,26 @@ enum {
   DSLPG_ERR_BAD_ARGUMENT = -5
 };
 
+/* Kernel-shape selection (normally DSLPG_PATH_AUTO; the others exist so tests
+ * and benchmarks can exercise one implementation on purpose). */
+enum {
+  DSLPG_PATH_AUTO = 0,     /* pick per shape */
+  DSLPG_PATH_RESIDENT = 1, /* rows read straight into registers */
+  DSLPG_PATH_TMA = 2,      /* rows / row chunks staged by TMA bulk copies */
+  DSLPG_PATH_STREAM = 3    /* two-pass streaming (any length or alignment) */
+};
+
+/* Select the kernel shape for subsequent calls (process-wide). A path that
+ * cannot handle a given shape falls back to one that can. Returns 0 or
+ * DSLPG_ERR_BAD_ARGUMENT. No reference counterpart: a testing aid. */
+DSLPG_API int dslpg_set_kernel_path(int path);
+
+/* Number of bounded device-side waits (TMA pipeline barriers) that ran out of
+ * time since the last call, and reset the count. Synchronises the device.
+ * A non-zero value means some outputs of the affected launches were not
+ * written. No reference counterpart. */
+DSLPG_API unsigned int dslpg_take_wait_timeouts(void);
+
 /* Library version, (major << 16) | minor. */
 DSLPG_API int dslpg_version(void);
 

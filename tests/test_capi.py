@@ -36,8 +36,16 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_python_binding_covers_header():
-    bound = set(_lib.SIGNATURES) | {"dslpg_error_string"}
+    bound = set(_lib.SIGNATURES) | {"dslpg_error_string", "dslpg_take_wait_timeouts"}
     assert set(declared_symbols()) <= bound
+
+
+def test_kernel_path_validation(lib):
+    assert lib.dslpg_set_kernel_path(9) == -5
+    assert lib.dslpg_set_kernel_path(-1) == -5
+    for code in range(4):
+        assert lib.dslpg_set_kernel_path(code) == 0
+    assert lib.dslpg_set_kernel_path(0) == 0
 
 
 def test_version(lib):

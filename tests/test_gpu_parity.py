@@ -20,6 +20,16 @@ from dslperfgap_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+PATHS = ["auto", "resident", "tma", "stream"]
+
+
+@pytest.fixture(params=PATHS)
+def path(request):
+    """Run the test under each kernel shape (shapes a path cannot take fall back)."""
+    with _lib.kernel_path(request.param):
+        yield request.param
+
+
 LENGTHS = [1, 7, 32, 64, 100, 128, 256, 512, 1000, 1024, 2048, 4096, 5120, 8192, 12288, 16384, 32768,
            40000, 65536, 131072]
 
@@ -43,7 +53,7 @@ def assert_parity(out, ref, dtype, normalised=False):
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("n", LENGTHS)
-def test_layer_norm_lengths(n, dt):
+def test_layer_norm_lengths(n, dt, path):
     g = gen(n)
     dtype = DT[dt]
     x = randn((rows_for(n), n), dtype, g)
@@ -56,7 +66,7 @@ def test_layer_norm_lengths(n, dt):
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("n", LENGTHS)
-def test_rms_norm_lengths(n, dt):
+def test_rms_norm_lengths(n, dt, path):
     g = gen(n + 1)
     dtype = DT[dt]
     x = randn((rows_for(n), n), dtype, g)
@@ -67,7 +77,7 @@ def test_rms_norm_lengths(n, dt):
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("n", LENGTHS)
-def test_softmax_lengths(n, dt):
+def test_softmax_lengths(n, dt, path):
     g = gen(n + 2)
     dtype = DT[dt]
     x = randn((rows_for(n), n), dtype, g, std=3.0)
@@ -77,7 +87,7 @@ def test_softmax_lengths(n, dt):
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("n", LENGTHS)
-def test_log_softmax_lengths(n, dt):
+def test_log_softmax_lengths(n, dt, path):
     g = gen(n + 3)
     dtype = DT[dt]
     x = randn((rows_for(n), n), dtype, g, std=3.0)
@@ -87,7 +97,7 @@ def test_log_softmax_lengths(n, dt):
 
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("n", LENGTHS + [128256])
-def test_logsumexp_lengths(n, dt):
+def test_logsumexp_lengths(n, dt, path):
     g = gen(n + 4)
     dtype = DT[dt]
     x = randn((rows_for(n), n), dtype, g, std=2.0)
@@ -117,9 +127,9 @@ def test_log_softmax_other_dims(shape, dim, dt):
 @pytest.mark.parametrize("bs", [1, 5, 64, 1000, 4096, 131072])
 @pytest.mark.parametrize("smooth,split", [(False, False), (True, False), (True, True), (False, True)])
 @pytest.mark.parametrize("dt", ["f32", "bf16"])
-def test_cross_entropy_blocks(bs, smooth, split, dt):
+def test_cross_entropy_blocks(bs, smooth, split, dt, path):
     g = gen(bs)
-    r, c = 16, 5000
+    r, c = 16, 40000
     lg = randn((r, c), DT[dt], g, std=2.0)
     lb = torch.randint(0, c, (r,), generator=g, dtype=torch.int64)
     lb[3] = -100
@@ -274,3 +284,9 @@ def test_current_stream_is_used():
         y = B.softmax(x)
     s.synchronize()
     assert_parity(y, oracle.softmax(x.cpu()), torch.float32)
+
+
+def test_no_pipeline_wait_ran_out():
+    """Run last in this file: no bounded device wait expired in any test above."""
+    torch.cuda.synchronize()
+    assert _lib.take_wait_timeouts() == 0
