@@ -11,6 +11,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/dslpg_b200.h"
 
 #define DSLPG_DEV __device__ __forceinline__
@@ -171,6 +173,155 @@ DSLPG_DEV float max_nan(float a, float b) {
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
   return r;
 }
+
+// Raw bit pattern of two -inf values of T in one 32-bit word (one for fp32).
+template <typename T> struct NegInfWord;
+template <> struct NegInfWord<float> { static constexpr uint32_t v = 0xff800000u; };
+template <> struct NegInfWord<__half> { static constexpr uint32_t v = 0xfc00fc00u; };
+template <> struct NegInfWord<__nv_bfloat16> { static constexpr uint32_t v = 0xff80ff80u; };
+
+// ----------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100a fma/add/mul .f32x2: two lanes per instruction)
+// ----------------------------------------------------------------------------
+typedef unsigned long long f32x2;
+
+DSLPG_DEV f32x2 pk2(float a, float b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+DSLPG_DEV void upk2(f32x2 v, float& a, float& b) { asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+DSLPG_DEV f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+DSLPG_DEV f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+DSLPG_DEV f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+DSLPG_DEV float hsum2(f32x2 v) {
+  float a, b;
+  upk2(v, a, b);
+  return a + b;
+}
+
+// Elements (2p, 2p+1) of a 16-byte vector of T as an fp32 pair,
+// p in [0, Elt<T>::kPerVec / 2).
+template <typename T> DSLPG_DEV f32x2 unpack_pair(const Vec16& v, int p);
+template <> DSLPG_DEV f32x2 unpack_pair<float>(const Vec16& v, int p) {
+  return pk2(__uint_as_float(v.w[2 * p]), __uint_as_float(v.w[2 * p + 1]));
+}
+template <> DSLPG_DEV f32x2 unpack_pair<__nv_bfloat16>(const Vec16& v, int p) {
+  return pk2(__uint_as_float(v.w[p] << 16), __uint_as_float(v.w[p] & 0xffff0000u));
+}
+template <> DSLPG_DEV f32x2 unpack_pair<__half>(const Vec16& v, int p) {
+  float2 t = __half22float2(*reinterpret_cast<const __half2*>(&v.w[p]));
+  return pk2(t.x, t.y);
+}
+
+// Store the 2P values of P fp32 pairs as 2P elements of T at p (aligned to
+// 2P * sizeof(T)), rounding to nearest even.
+template <typename T, int P> struct StorePairs;
+template <int P> struct StorePairs<float, P> {
+  static DSLPG_DEV void run(void* p, const f32x2* y) {
+#pragma unroll
+    for (int q = 0; q < P / 2; ++q) {
+      float a, b, c, d;
+      upk2(y[2 * q], a, b);
+      upk2(y[2 * q + 1], c, d);
+      st_stream(static_cast<char*>(p) + 16 * q,
+                Vec16{{__float_as_uint(a), __float_as_uint(b), __float_as_uint(c), __float_as_uint(d)}});
+    }
+  }
+};
+template <typename T16, int P> struct StorePairs16 {
+  static DSLPG_DEV void run(void* p, const f32x2* y) {
+    uint32_t w[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      float a, b;
+      upk2(y[i], a, b);
+      w[i] = pack2<T16>(a, b);
+    }
+    if constexpr (P == 2) st_stream8(p, w[0], w[1]);
+    else st_stream(p, Vec16{{w[0], w[1], w[2], w[3]}});
+  }
+};
+template <int P> struct StorePairs<__half, P> : StorePairs16<__half, P> {};
+template <int P> struct StorePairs<__nv_bfloat16, P> : StorePairs16<__nv_bfloat16, P> {};
+
+// Largest (MIN: smallest) element of NV vectors of T, compared on the stored
+// values (16-bit values two per instruction, fp32 three-input), as fp32;
+// NaN-propagating.
+template <typename T, int NV, bool MIN> struct RawExtreme;
+template <int NV, bool MIN> struct RawExtreme<float, NV, MIN> {
+  static DSLPG_DEV float op3(float a, float b, float c) {
+    float r;
+    if constexpr (MIN) asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    else asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+  }
+  static DSLPG_DEV float run(const Vec16 (&v)[NV]) {
+    float f[4 * NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) f[4 * k + i] = __uint_as_float(v[k].w[i]);
+    // a tree of three-input steps
+#pragma unroll
+    for (int n = 4 * NV; n > 1; n = (n + 2) / 3) {
+#pragma unroll
+      for (int i = 0; i < (n + 2) / 3; ++i) {
+        const float a = f[3 * i];
+        const float b = (3 * i + 1 < n) ? f[3 * i + 1] : a;
+        const float c = (3 * i + 2 < n) ? f[3 * i + 2] : a;
+        f[i] = op3(a, b, c);
+      }
+    }
+    return f[0];
+  }
+};
+template <typename T16, int NV, bool MIN> struct RawExtreme16 {
+  static DSLPG_DEV uint32_t op(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (std::is_same<T16, __nv_bfloat16>::value) {
+      if constexpr (MIN) asm("min.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+      else asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    } else {
+      if constexpr (MIN) asm("min.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+      else asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    }
+    return r;
+  }
+  static DSLPG_DEV float run(const Vec16 (&v)[NV]) {
+    uint32_t w[4 * NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[4 * k + i] = v[k].w[i];
+#pragma unroll
+    for (int n = 4 * NV; n > 1; n = (n + 1) / 2) {
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) w[i] = op(w[2 * i], w[2 * i + 1]);
+      if (n & 1) w[n / 2] = w[n - 1];
+    }
+    const f32x2 pr = unpack_pair<T16>(Vec16{{w[0], 0u, 0u, 0u}}, 0);
+    float a, b, r;
+    upk2(pr, a, b);
+    if constexpr (MIN) asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    else asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+  }
+};
+template <int NV, bool MIN> struct RawExtreme<__nv_bfloat16, NV, MIN> : RawExtreme16<__nv_bfloat16, NV, MIN> {};
+template <int NV, bool MIN> struct RawExtreme<__half, NV, MIN> : RawExtreme16<__half, NV, MIN> {};
 
 struct SumOp {
   static DSLPG_DEV float identity() { return 0.f; }

@@ -40,6 +40,7 @@ struct RowArgs {
   int tpr;    // threads per row
   int rpc;    // rows per CTA (resident kernel)
   float eps;
+  float inv_n;  // 1 / N
   int wdt;    // weight dtype code
   int wvec;   // 1: weight/bias have x's dtype and are 16-byte aligned
 };
@@ -69,152 +70,177 @@ DSLPG_DEV void load_weight(const void* p, int j, float* out) {
 // ============================================================================
 // Per-row math shared by the resident and TMA kernels
 // ============================================================================
+// Weight (or bias) vector j of a row as raw 16-byte data (zeros if p is null).
+// Read through L1: every row of a CTA reads the same vectors.
+template <typename Tin>
+DSLPG_DEV Vec16 weight_vec(const void* p, int j) {
+  if (p == nullptr) return Vec16{{0u, 0u, 0u, 0u}};
+  return ld_keep(static_cast<const Tin*>(p) + static_cast<int64_t>(j) * Elt<Tin>::kPerVec);
+}
+
 // Normalise one row whose VPT 16-byte vectors (elements [j*E, j*E+E) with
-// j = t + k*tpr) this thread holds in v; masked vectors hold zeros. Stores the
-// thread's part of the output row yr. Every thread of the row group calls it.
+// j = t + k*tpr) this thread holds in v; masked vectors (ok[k] false, always
+// the trailing ones) hold zeros. Stores the thread's part of the output row
+// yr. Every thread of the row group calls it. Element arithmetic runs on fp32
+// pairs, two lanes per fma/add/mul.f32x2 instruction.
 template <int OP, typename Tin, typename Tout, int VPT, int CACHE_LIMIT, class Red>
 DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool (&ok)[VPT], int t,
                              Tout* yr, Red& rd) {
   constexpr int E = Elt<Tin>::kPerVec;
+  constexpr int P = E / 2;
   // Up to CACHE_LIMIT fp32 values per thread are kept unpacked (softmax keeps
   // the exp values there, so each element costs one ex2); longer slices stay
   // packed and are unpacked again in each phase.
   constexpr bool kCache = VPT * E <= CACHE_LIMIT;
-  const float n_f = static_cast<float>(a.N);
 
-  float fr[kCache ? VPT : 1][E];
+  auto load_pair = [&](int k, int p) -> f32x2 {
+    f32x2 x = unpack_pair<Tin>(v[k], p);
+    if constexpr (kRoundIn<Tin, Tout>) {
+      float x0, x1;
+      upk2(x, x0, x1);
+      x = pk2(round_to<Tout>(x0), round_to<Tout>(x1));
+    }
+    return x;
+  };
+  f32x2 fr[kCache ? VPT : 1][P];
   if constexpr (kCache) {
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      unpack<Tin>(v[k], fr[k]);
+    for (int k = 0; k < VPT; ++k)
 #pragma unroll
-      for (int i = 0; i < E; ++i) fr[k][i] = in_value<Tin, Tout>(fr[k][i]);
-    }
+      for (int p = 0; p < P; ++p) fr[k][p] = load_pair(k, p);
   }
-  // The fp32 values of vector k (masked vectors read as 0).
-  auto get = [&](int k, float* f) {
-    if constexpr (kCache) {
-#pragma unroll
-      for (int i = 0; i < E; ++i) f[i] = fr[k][i];
-    } else {
-      unpack<Tin>(v[k], f);
-#pragma unroll
-      for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
-    }
+  auto pair = [&](int k, int p) -> f32x2 {
+    if constexpr (kCache) return fr[k][p];
+    else return load_pair(k, p);
+  };
+  auto store = [&](int k, const f32x2 (&y)[P]) {
+    StorePairs<Tout, P>::run(yr + static_cast<int64_t>(t + k * a.tpr) * E, y);
   };
 
   if constexpr (OP == kRmsNorm) {
-    float ss = 0.f;
+    f32x2 ss2 = pk2(0.f, 0.f);
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      float f[E];
-      get(k, f);
+    for (int k = 0; k < VPT; ++k)
 #pragma unroll
-      for (int i = 0; i < E; ++i) ss = fmaf(f[i], f[i], ss);
-    }
-    ss = rd.template reduce<SumOp>(ss);
-    const float inv = 1.0f / sqrtf(ss / n_f + a.eps);
+      for (int p = 0; p < P; ++p) {
+        const f32x2 x = pair(k, p);
+        ss2 = fma2(x, x, ss2);
+      }
+    const float ss = rd.template reduce<SumOp>(hsum2(ss2));
+    const float inv = rsqrtf(ss * a.inv_n + a.eps);
+    const f32x2 inv2 = pk2(inv, inv);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       if (!ok[k]) continue;
-      const int j = t + k * a.tpr;
-      float f[E], w[E];
-      get(k, f);
-      load_weight<Tin, E>(a.w, j, w);
+      const Vec16 wk = weight_vec<Tin>(a.w, t + k * a.tpr);
+      f32x2 y[P];
 #pragma unroll
-      for (int i = 0; i < E; ++i) f[i] = (f[i] * inv) * w[i];
-      StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+      for (int p = 0; p < P; ++p) y[p] = mul2(mul2(pair(k, p), inv2), unpack_pair<Tin>(wk, p));
+      store(k, y);
     }
   } else if constexpr (OP == kLayerNorm) {
-    float s = 0.f;
+    f32x2 s2 = pk2(0.f, 0.f);
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      float f[E];
-      get(k, f);
+    for (int k = 0; k < VPT; ++k)
 #pragma unroll
-      for (int i = 0; i < E; ++i) s += f[i];
-    }
-    s = rd.template reduce<SumOp>(s);
-    const float mean = s / n_f;
-    float q = 0.f;
+      for (int p = 0; p < P; ++p) s2 = add2(s2, pair(k, p));
+    const float mean = rd.template reduce<SumOp>(hsum2(s2)) * a.inv_n;
+    const f32x2 nmean2 = pk2(-mean, -mean);
+    f32x2 q2 = pk2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       if (!ok[k]) continue;
-      float f[E];
-      get(k, f);
 #pragma unroll
-      for (int i = 0; i < E; ++i) {
-        const float d = f[i] - mean;
-        q = fmaf(d, d, q);
+      for (int p = 0; p < P; ++p) {
+        const f32x2 d = add2(pair(k, p), nmean2);
+        q2 = fma2(d, d, q2);
       }
     }
-    q = rd.template reduce<SumOp>(q);
-    const float rstd = 1.0f / sqrtf(q / n_f + a.eps);
+    const float var = rd.template reduce<SumOp>(hsum2(q2)) * a.inv_n;
+    const float rstd = rsqrtf(var + a.eps);
+    const f32x2 rstd2 = pk2(rstd, rstd);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       if (!ok[k]) continue;
       const int j = t + k * a.tpr;
-      float f[E], w[E], bb[E];
-      get(k, f);
-      load_weight<Tin, E>(a.w, j, w);
-      load_weight<Tin, E>(a.b, j, bb);
+      const Vec16 wk = weight_vec<Tin>(a.w, j), bk = weight_vec<Tin>(a.b, j);
+      f32x2 y[P];
 #pragma unroll
-      for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - mean) * rstd, w[i], bb[i]);
-      StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+      for (int p = 0; p < P; ++p)
+        y[p] = fma2(mul2(add2(pair(k, p), nmean2), rstd2), unpack_pair<Tin>(wk, p), unpack_pair<Tin>(bk, p));
+      store(k, y);
     }
   } else {  // kSoftmax / kLogSoftmax
-    float m = kNegInf;
+    float m;
+    if constexpr (!kRoundIn<Tin, Tout>) {
+      // max on the stored values; masked vectors count as -inf
+      if (ok[VPT - 1]) {
+        m = RawExtreme<Tin, VPT, false>::run(v);
+      } else {
+        constexpr uint32_t ni = NegInfWord<Tin>::v;
+        Vec16 vm[VPT];
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      if (!ok[k]) continue;
-      float f[E];
-      get(k, f);
-#pragma unroll
-      for (int i = 0; i < E; ++i) m = max_nan(m, f[i]);
-    }
-    m = rd.template reduce<MaxOp>(m);
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      if (!ok[k]) continue;
-      float f[E];
-      get(k, f);
-#pragma unroll
-      for (int i = 0; i < E; ++i) {
-        const float e = exp_shifted(f[i] - m);
-        if constexpr (kCache && OP == kSoftmax) fr[k][i] = e;
-        s += e;
+        for (int k = 0; k < VPT; ++k) vm[k] = ok[k] ? v[k] : Vec16{{ni, ni, ni, ni}};
+        m = RawExtreme<Tin, VPT, false>::run(vm);
       }
-    }
-    s = rd.template reduce<SumOp>(s);
-    if constexpr (OP == kSoftmax) {
-      const float inv = 1.0f / s;
+    } else {
+      m = kNegInf;
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         if (!ok[k]) continue;
-        const int j = t + k * a.tpr;
-        float f[E];
-        if constexpr (kCache) {
 #pragma unroll
-          for (int i = 0; i < E; ++i) f[i] = fr[k][i] * inv;
-        } else {
-          get(k, f);
-#pragma unroll
-          for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - m) * inv;
+        for (int p = 0; p < P; ++p) {
+          float x0, x1;
+          upk2(pair(k, p), x0, x1);
+          m = max_nan(m, max_nan(x0, x1));
         }
-        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+      }
+    }
+    m = rd.template reduce<MaxOp>(m);
+    const f32x2 nm2 = pk2(-m, -m), l2e2 = pk2(kLog2e, kLog2e);
+    f32x2 s2 = pk2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!ok[k]) continue;
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        float t0, t1;
+        upk2(mul2(add2(pair(k, p), nm2), l2e2), t0, t1);
+        const f32x2 e = pk2(ex2(t0), ex2(t1));
+        if constexpr (kCache && OP == kSoftmax) fr[k][p] = e;
+        s2 = add2(s2, e);
+      }
+    }
+    const float s = rd.template reduce<SumOp>(hsum2(s2));
+    if constexpr (OP == kSoftmax) {
+      const float inv = 1.0f / s;
+      const f32x2 inv2 = pk2(inv, inv);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+        f32x2 y[P];
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          if constexpr (kCache) {
+            y[p] = mul2(fr[k][p], inv2);
+          } else {
+            float t0, t1;
+            upk2(mul2(add2(pair(k, p), nm2), l2e2), t0, t1);
+            y[p] = mul2(pk2(ex2(t0), ex2(t1)), inv2);
+          }
+        }
+        store(k, y);
       }
     } else {
       const float ls = logf(s);
+      const f32x2 nls2 = pk2(-ls, -ls);
 #pragma unroll
       for (int k = 0; k < VPT; ++k) {
         if (!ok[k]) continue;
-        const int j = t + k * a.tpr;
-        float f[E];
-        get(k, f);
+        f32x2 y[P];
 #pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = (f[i] - m) - ls;
-        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+        for (int p = 0; p < P; ++p) y[p] = add2(add2(pair(k, p), nm2), nls2);
+        store(k, y);
       }
     }
   }
@@ -739,6 +765,7 @@ RowArgs make_args(const void* x, void* y, const void* w, const void* b, int64_t 
   a.M = M;
   a.N = static_cast<int>(N);
   a.eps = eps;
+  a.inv_n = 1.0f / static_cast<float>(N);
   a.wdt = w_dt;
   a.wvec = (w != nullptr && w_dt == x_dt && aligned(w, 16) && (b == nullptr || aligned(b, 16)))
                ? 1

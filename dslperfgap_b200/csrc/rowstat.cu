@@ -62,6 +62,62 @@ DSLPG_DEV void fold_chunk(float& m, float& s, const float* t) {
 
 // Write the results of work item (row r, block cb) from the merged online
 // statistics: gm = max of t, gs = sum of 2^(t - gm), gsum = sum of x (SMOOTH).
+// Fold NV full 16-byte vectors of T (every element valid) into the running
+// (m, s) of t = x * c in the log2 domain; with SMOOTH also add the plain sum of
+// x to `sum`. The chunk's extreme is found on the stored values (two 16-bit
+// values per instruction); each element then costs half an fma.f32x2, one
+// ex2 and half an add.f32x2. x * c - m is formed with a single rounding (fma),
+// so the largest element contributes 2^r with |r| at most half an ulp of m.
+template <typename T, int NV, bool SMOOTH>
+DSLPG_DEV void fold_vecs(float& m, float& s, float& sum, const Vec16 (&v)[NV], float c) {
+  constexpr int P = Elt<T>::kPerVec / 2;
+  if constexpr (SMOOTH) {
+    f32x2 s2 = pk2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int p = 0; p < P; ++p) s2 = add2(s2, unpack_pair<T>(v[k], p));
+    sum += hsum2(s2);
+  }
+  // max(x * c) is c * max(x) for c >= 0 and c * min(x) for c < 0 (rounding
+  // is monotonic); c == 0 gives 0 (NaN for non-finite x), as x * 0 does.
+  const float ext = (c >= 0.f) ? RawExtreme<T, NV, false>::run(v) : RawExtreme<T, NV, true>::run(v);
+  const float nm = max_nan(m, ext * c);
+  if (nm == kNegInf) return;  // nothing but -inf so far
+  const f32x2 c2 = pk2(c, c), nnm2 = pk2(-nm, -nm);
+  f32x2 acc0 = pk2(0.f, 0.f), acc1 = pk2(0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      float d0, d1;
+      upk2(fma2(unpack_pair<T>(v[k], p), c2, nnm2), d0, d1);
+      if ((k * P + p) & 1) acc1 = add2(acc1, pk2(ex2(d0), ex2(d1)));
+      else acc0 = add2(acc0, pk2(ex2(d0), ex2(d1)));
+    }
+  s = ((m == nm) ? s : s * ex2(m - nm)) + hsum2(add2(acc0, acc1));
+  m = nm;
+}
+
+// fold_vecs for a partial chunk: vectors with ok[k] false are left out.
+template <typename T, int NV, bool SMOOTH>
+DSLPG_DEV void fold_vecs_masked(float& m, float& s, float& sum, const Vec16 (&v)[NV], const bool (&ok)[NV],
+                                float c) {
+  constexpr int E = Elt<T>::kPerVec;
+  float tv[NV * E];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    float f[E];
+    unpack<T>(v[k], f);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      tv[k * E + i] = ok[k] ? f[i] * c : kNegInf;
+      if constexpr (SMOOTH) sum += ok[k] ? f[i] : 0.f;
+    }
+  }
+  fold_chunk<NV * E>(m, s, tv);
+}
+
 template <int KIND, typename T, bool SMOOTH>
 DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col0, float gm, float gs,
                            float gsum) {
@@ -104,7 +160,7 @@ DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col
 }
 
 template <int KIND, typename T, int V, bool SMOOTH>
-__global__ void __launch_bounds__(1024) rowstat_kernel(const StatArgs a) {
+__global__ void __launch_bounds__(256) rowstat_kernel(const StatArgs a) {
   constexpr int U = (V == 1) ? 8 : 4;  // loads in flight per thread per iteration
   __shared__ float red[2][32];
   const int g = threadIdx.x / a.tpr;
@@ -136,19 +192,11 @@ __global__ void __launch_bounds__(1024) rowstat_kernel(const StatArgs a) {
           v[u] = Vec16{{0u, 0u, 0u, 0u}};
           if (j < nv) v[u] = ld_stream(xs + j * V);
         }
-        float tv[U * V];
+        bool ok[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t j = j0 + static_cast<int64_t>(u) * a.tpr;
-          float f[V];
-          unpack<T>(v[u], f);
-#pragma unroll
-          for (int i = 0; i < V; ++i) {
-            if constexpr (SMOOTH) sum += f[i];  // masked vectors read as 0
-            tv[u * V + i] = (j < nv) ? f[i] * a.c : kNegInf;
-          }
-        }
-        fold_chunk<U * V>(m, s, tv);
+        for (int u = 0; u < U; ++u) ok[u] = j0 + static_cast<int64_t>(u) * a.tpr < nv;
+        if (ok[U - 1]) fold_vecs<T, U, SMOOTH>(m, s, sum, v, a.c);
+        else fold_vecs_masked<T, U, SMOOTH>(m, s, sum, v, ok, a.c);
       }
       done = nv * V;
     }
@@ -193,7 +241,7 @@ static __device__ unsigned int g_wait_timeouts;
 // handled as in the normalising TMA kernel: the loop shape never changes, so
 // the consumers' named barriers stay matched.
 template <int KIND, typename T, bool SMOOTH>
-__global__ void __launch_bounds__(1024) tma_stat_kernel(const StatArgs a, int stages, uint32_t chunk_bytes,
+__global__ void __launch_bounds__(288) tma_stat_kernel(const StatArgs a, int stages, uint32_t chunk_bytes,
                                                         unsigned long long limit_ns) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int E = Elt<T>::kPerVec;
@@ -261,19 +309,11 @@ __global__ void __launch_bounds__(1024) tma_stat_kernel(const StatArgs a, int st
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(ring.empty_bar(u));
-      float tv[VPC * E];
+      bool ok[VPC];
 #pragma unroll
-      for (int k = 0; k < VPC; ++k) {
-        const bool ok = static_cast<uint32_t>(t + k * C) < nv;
-        float f[E];
-        unpack<T>(v[k], f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          if constexpr (SMOOTH) sum += f[i];  // masked vectors read as 0
-          tv[k * E + i] = ok ? f[i] * a.c : kNegInf;
-        }
-      }
-      fold_chunk<VPC * E>(m, s, tv);
+      for (int k = 0; k < VPC; ++k) ok[k] = static_cast<uint32_t>(t + k * C) < nv;
+      if (ok[VPC - 1]) fold_vecs<T, VPC, SMOOTH>(m, s, sum, v, a.c);
+      else fold_vecs_masked<T, VPC, SMOOTH>(m, s, sum, v, ok, a.c);
     }
     const float gm = rd.template reduce<MaxOp>(m);
     const float sc = (m == gm) ? s : s * ex2(m - gm);
