@@ -346,11 +346,10 @@ cudaError_t launch_stat(StatArgs a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// TMA path: work items of at least kTmaMinItem bytes, streamed in chunks of
+// TMA path (selected explicitly): work items streamed in chunks of
 // kTmaChunk bytes through a ring of kTmaStages slots (two CTAs per SM).
 constexpr uint32_t kTmaChunk = 16u * 1024u;
 constexpr int kTmaStages = 6;
-constexpr int64_t kTmaMinItem = 32 * 1024;
 constexpr int kTmaConsumers = 256;
 
 template <int KIND, typename T, bool SMOOTH>
@@ -374,8 +373,8 @@ cudaError_t dispatch_vec(StatArgs a, cudaStream_t st) {
   // every item's byte count must be a multiple of 16 for the bulk copies
   const bool tma_ok = vec && (a.N % E == 0);
   const int64_t item_bytes = a.seg * static_cast<int64_t>(sizeof(T));
-  if (tma_ok && path != DSLPG_PATH_RESIDENT && path != DSLPG_PATH_STREAM &&
-      (item_bytes >= kTmaMinItem || path == DSLPG_PATH_TMA))
+  // Explicit selection only: the register kernel is measured faster on B200.
+  if (tma_ok && path == DSLPG_PATH_TMA && item_bytes > 0)
     return launch_tma_stat<KIND, T, SMOOTH>(a, st);
   if (vec && path != DSLPG_PATH_STREAM) return launch_stat<KIND, T, E, SMOOTH>(a, st);
   return launch_stat<KIND, T, 1, SMOOTH>(a, st);
