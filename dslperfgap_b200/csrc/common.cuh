@@ -323,6 +323,36 @@ template <typename T16, int NV, bool MIN> struct RawExtreme16 {
 template <int NV, bool MIN> struct RawExtreme<__nv_bfloat16, NV, MIN> : RawExtreme16<__nv_bfloat16, NV, MIN> {};
 template <int NV, bool MIN> struct RawExtreme<__half, NV, MIN> : RawExtreme16<__half, NV, MIN> {};
 
+// 2^d for both lanes of a pair on the FMA and integer pipes, leaving the SFU
+// free (used for a share of the exponentials of the long-row reductions, whose
+// throughput is otherwise bounded by the SFU). Method: d = n + f with
+// n = round(d) (added to 1.5 * 2^23, whose low mantissa bits then hold n) and
+// |f| <= 1/2; 2^f from a degree-4 polynomial whose coefficients were fitted
+// for this library by iteratively reweighted least squares on Chebyshev nodes
+// (max relative error 2.7e-6 in fp32 over [-1/2, 1/2]); n is added to the
+// exponent field. Lanes below -126 are clamped there: their 2^d < 1.2e-38 is
+// negligible next to the 1 of the largest term; a NaN lane becomes a finite
+// value, which callers tolerate because a NaN already poisons the running
+// maximum (see fold_vecs).
+DSLPG_DEV f32x2 exp2_poly2(f32x2 d) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  float d0, d1;
+  upk2(d, d0, d1);
+  const f32x2 dc = pk2(fmaxf(d0, -126.0f), fmaxf(d1, -126.0f));
+  const f32x2 t = add2(dc, pk2(kRound, kRound));
+  const f32x2 n = add2(t, pk2(-kRound, -kRound));
+  const f32x2 f = fma2(n, pk2(-1.0f, -1.0f), dc);
+  f32x2 p = fma2(pk2(0.009570095f, 0.009570095f), f, pk2(0.05591786f, 0.05591786f));
+  p = fma2(p, f, pk2(0.24024744f, 0.24024744f));
+  p = fma2(p, f, pk2(0.69312179f, 0.69312179f));
+  p = fma2(p, f, pk2(0.99999928f, 0.99999928f));
+  float t0, t1, p0, p1;
+  upk2(t, t0, t1);
+  upk2(p, p0, p1);
+  return pk2(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
+             __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
+}
+
 struct SumOp {
   static DSLPG_DEV float identity() { return 0.f; }
   static DSLPG_DEV float apply(float a, float b) { return a + b; }

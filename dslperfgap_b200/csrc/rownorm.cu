@@ -249,12 +249,11 @@ DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool
 // ============================================================================
 // Resident kernel: rows read straight into registers
 // ============================================================================
-template <int OP, typename Tin, typename Tout, int VPT>
+// PD = rows loaded ahead of the one being reduced (0, 1 or 2), so that every
+// thread keeps PD rows of loads in flight while it reduces.
+template <int OP, typename Tin, typename Tout, int VPT, int PD>
 __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
   constexpr int E = Elt<Tin>::kPerVec;
-  // With <= 4 vectors per thread the next row's vectors are loaded before this
-  // row is reduced, so every thread always has loads in flight.
-  constexpr bool kPrefetch = VPT <= 4;
   __shared__ float red[2][32];
 
   const int g = threadIdx.x / a.tpr;
@@ -272,24 +271,35 @@ __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
   };
 
   const int64_t step = static_cast<int64_t>(gridDim.x) * a.rpc;
-  Vec16 nxt[kPrefetch ? VPT : 1];
-  if constexpr (kPrefetch) load_row(nxt, static_cast<int64_t>(blockIdx.x) * a.rpc + g);
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * a.rpc + g;
+  Vec16 q0[PD >= 1 ? VPT : 1], q1[PD >= 2 ? VPT : 1];
+  if constexpr (PD >= 1) load_row(q0, first);
+  if constexpr (PD >= 2) load_row(q1, first + step);
 
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * a.rpc; base < a.M; base += step) {
     const int64_t row = base + g;
     Vec16 v[VPT];
-    if constexpr (kPrefetch) {
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) v[k] = nxt[k];
-      load_row(nxt, row + step);
-    } else {
+    if constexpr (PD == 0) {
       load_row(v, row);
+    } else {
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) v[k] = q0[k];
+      if constexpr (PD == 2) {
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) q0[k] = q1[k];
+        load_row(q1, row + 2 * step);
+      } else {
+        load_row(q0, row + step);
+      }
     }
     bool ok[VPT];
 #pragma unroll
     for (int k = 0; k < VPT; ++k) ok[k] = row < a.M && (t + k * a.tpr) < a.nvec;
-    // 16 cached values: the prefetch buffer needs the other registers.
-    normalize_row<OP, Tin, Tout, VPT, 16>(a, v, ok, t, static_cast<Tout*>(a.y) + row * a.N, rd);
+    // 16 cached values: the prefetch buffers need the other registers.
+    // log_softmax re-reads x in its output phase: recomputing the unpack there
+    // is cheaper than the registers a cached copy costs in occupancy.
+    normalize_row<OP, Tin, Tout, VPT, (OP == kLogSoftmax ? 0 : 16)>(a, v, ok, t,
+                                                                    static_cast<Tout*>(a.y) + row * a.N, rd);
   }
 }
 
@@ -627,14 +637,14 @@ namespace {
 
 inline int round_up32(int v) { return (v + 31) & ~31; }
 
-template <int OP, typename Tin, typename Tout, int VPT>
+template <int OP, typename Tin, typename Tout, int VPT, int PD = (VPT <= 4 ? 1 : 0)>
 cudaError_t launch_resident(RowArgs a, cudaStream_t st) {
   a.tpr = round_up32((a.nvec + VPT - 1) / VPT);
   a.rpc = a.tpr >= 256 ? 1 : 256 / a.tpr;
   const int block = a.tpr * a.rpc;
-  const void* fn = reinterpret_cast<const void*>(&resident_kernel<OP, Tin, Tout, VPT>);
+  const void* fn = reinterpret_cast<const void*>(&resident_kernel<OP, Tin, Tout, VPT, PD>);
   const int grid = persistent_grid(fn, block, 0, (a.M + a.rpc - 1) / a.rpc);
-  resident_kernel<OP, Tin, Tout, VPT><<<grid, block, 0, st>>>(a);
+  resident_kernel<OP, Tin, Tout, VPT, PD><<<grid, block, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -704,11 +714,20 @@ cudaError_t dispatch_rows(RowArgs a, cudaStream_t st) {
       // About 16 elements per thread (4 fp32 or 2 16-bit vectors), more only
       // when the row would need more than 1024 threads, fewer for short rows.
       constexpr int kBase = (E == 4) ? 4 : 2;
+      // log_softmax: 32 elements per thread measured faster (fewer threads
+      // per row to reduce over; its element work is the lightest).
+      if constexpr (OP == kLogSoftmax && E == 8) {
+        if (a.nvec >= 128 && a.nvec <= 4 * 1024) return launch_resident<OP, Tin, Tout, 4>(a, st);
+      }
       if constexpr (E == 4) {
         if (a.nvec > 4 * 1024) return launch_resident<OP, Tin, Tout, 8>(a, st);
       }
       if (a.nvec > kBase * 1024) return launch_resident<OP, Tin, Tout, 4>(a, st);
-      if (a.nvec >= 32 * kBase) return launch_resident<OP, Tin, Tout, kBase>(a, st);
+      if (a.nvec >= 32 * kBase) {
+        // softmax: two rows of loads in flight (free in registers at its occupancy)
+        if constexpr (OP == kSoftmax && kBase == 2) return launch_resident<OP, Tin, Tout, 2, 2>(a, st);
+        return launch_resident<OP, Tin, Tout, kBase>(a, st);
+      }
       if (a.nvec > 32) return launch_resident<OP, Tin, Tout, 2>(a, st);
       return launch_resident<OP, Tin, Tout, 1>(a, st);
     }

@@ -68,7 +68,7 @@ DSLPG_DEV void fold_chunk(float& m, float& s, const float* t) {
 // values per instruction); each element then costs half an fma.f32x2, one
 // ex2 and half an add.f32x2. x * c - m is formed with a single rounding (fma),
 // so the largest element contributes 2^r with |r| at most half an ulp of m.
-template <typename T, int NV, bool SMOOTH>
+template <typename T, int NV, bool SMOOTH, int POLY = 0>
 DSLPG_DEV void fold_vecs(float& m, float& s, float& sum, const Vec16 (&v)[NV], float c) {
   constexpr int P = Elt<T>::kPerVec / 2;
   if constexpr (SMOOTH) {
@@ -90,10 +90,17 @@ DSLPG_DEV void fold_vecs(float& m, float& s, float& sum, const Vec16 (&v)[NV], f
   for (int k = 0; k < NV; ++k)
 #pragma unroll
     for (int p = 0; p < P; ++p) {
-      float d0, d1;
-      upk2(fma2(unpack_pair<T>(v[k], p), c2, nnm2), d0, d1);
-      if ((k * P + p) & 1) acc1 = add2(acc1, pk2(ex2(d0), ex2(d1)));
-      else acc0 = add2(acc0, pk2(ex2(d0), ex2(d1)));
+      const f32x2 d = fma2(unpack_pair<T>(v[k], p), c2, nnm2);
+      f32x2 e;
+      if (POLY > 0 && (k * P + p) % POLY == POLY - 1) {
+        e = exp2_poly2(d);  // every POLY-th pair on the FMA pipe
+      } else {
+        float d0, d1;
+        upk2(d, d0, d1);
+        e = pk2(ex2(d0), ex2(d1));
+      }
+      if ((k * P + p) & 1) acc1 = add2(acc1, e);
+      else acc0 = add2(acc0, e);
     }
   s = ((m == nm) ? s : s * ex2(m - nm)) + hsum2(add2(acc0, acc1));
   m = nm;
@@ -159,9 +166,9 @@ DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col
   }
 }
 
-template <int KIND, typename T, int V, bool SMOOTH>
-__global__ void __launch_bounds__(256) rowstat_kernel(const StatArgs a) {
-  constexpr int U = (V == 1) ? 8 : 4;  // loads in flight per thread per iteration
+template <int KIND, typename T, int V, bool SMOOTH, int POLY, bool PF = false, int UV = 4, int MINB = 1>
+__global__ void __launch_bounds__(256, MINB) rowstat_kernel(const StatArgs a) {
+  constexpr int U = (V == 1) ? 8 : UV;  // loads in flight per thread per iteration
   __shared__ float red[2][32];
   const int g = threadIdx.x / a.tpr;
   const int t = threadIdx.x - g * a.tpr;
@@ -184,18 +191,30 @@ __global__ void __launch_bounds__(256) rowstat_kernel(const StatArgs a) {
     int64_t done = 0;
     if constexpr (V > 1) {
       const int64_t nv = len / V;
-      for (int64_t j0 = t; j0 < nv; j0 += static_cast<int64_t>(U) * a.tpr) {
-        Vec16 v[U];
+      const int64_t stride = static_cast<int64_t>(U) * a.tpr;
+      auto load = [&](Vec16 (&dst)[U], int64_t j0) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int64_t j = j0 + static_cast<int64_t>(u) * a.tpr;
-          v[u] = Vec16{{0u, 0u, 0u, 0u}};
-          if (j < nv) v[u] = ld_stream(xs + j * V);
+          dst[u] = Vec16{{0u, 0u, 0u, 0u}};
+          if (j < nv) dst[u] = ld_stream(xs + j * V);
+        }
+      };
+      Vec16 nx[PF ? U : 1];
+      if constexpr (PF) load(nx, t);
+      for (int64_t j0 = t; j0 < nv; j0 += stride) {
+        Vec16 v[U];
+        if constexpr (PF) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) v[u] = nx[u];
+          if (j0 + stride < nv) load(nx, j0 + stride);
+        } else {
+          load(v, j0);
         }
         bool ok[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) ok[u] = j0 + static_cast<int64_t>(u) * a.tpr < nv;
-        if (ok[U - 1]) fold_vecs<T, U, SMOOTH>(m, s, sum, v, a.c);
+        if (ok[U - 1]) fold_vecs<T, U, SMOOTH, POLY>(m, s, sum, v, a.c);
         else fold_vecs_masked<T, U, SMOOTH>(m, s, sum, v, ok, a.c);
       }
       done = nv * V;
@@ -240,12 +259,11 @@ static __device__ unsigned int g_wait_timeouts;
 // thread per chunk), release the slot, and merge per item. Timeouts are
 // handled as in the normalising TMA kernel: the loop shape never changes, so
 // the consumers' named barriers stay matched.
-template <int KIND, typename T, bool SMOOTH>
-__global__ void __launch_bounds__(288) tma_stat_kernel(const StatArgs a, int stages, uint32_t chunk_bytes,
+template <int KIND, typename T, bool SMOOTH, int VPC>
+__global__ void __launch_bounds__(544) tma_stat_kernel(const StatArgs a, int stages, uint32_t chunk_bytes,
                                                         unsigned long long limit_ns) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int E = Elt<T>::kPerVec;
-  constexpr int VPC = 4;
   __shared__ volatile int abort_flag;
   const int ncw = (blockDim.x >> 5) - 1;
   const int C = ncw * 32;
@@ -328,7 +346,7 @@ namespace {
 
 inline int round_up32(int v) { return (v + 31) & ~31; }
 
-template <int KIND, typename T, int V, bool SMOOTH>
+template <int KIND, typename T, int V, bool SMOOTH, int POLY = 0, bool PF = false, int UV = 4, int MINB = 1>
 cudaError_t launch_stat(StatArgs a, cudaStream_t st) {
   // Threads per work item: about 16 vectors (or 64 scalars) per thread per item.
   const int64_t units = (V > 1) ? a.seg / V : a.seg;
@@ -339,10 +357,10 @@ cudaError_t launch_stat(StatArgs a, cudaStream_t st) {
   a.tpr = tpr;
   a.rpc = tpr >= 256 ? 1 : 256 / tpr;
   const int block = a.tpr * a.rpc;
-  const void* fn = reinterpret_cast<const void*>(&rowstat_kernel<KIND, T, V, SMOOTH>);
+  const void* fn = reinterpret_cast<const void*>(&rowstat_kernel<KIND, T, V, SMOOTH, POLY, PF, UV, MINB>);
   const int64_t items = a.M * a.nseg;
   const int grid = persistent_grid(fn, block, 0, (items + a.rpc - 1) / a.rpc);
-  rowstat_kernel<KIND, T, V, SMOOTH><<<grid, block, 0, st>>>(a);
+  rowstat_kernel<KIND, T, V, SMOOTH, POLY, PF, UV, MINB><<<grid, block, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -352,17 +370,22 @@ constexpr uint32_t kTmaChunk = 16u * 1024u;
 constexpr int kTmaStages = 6;
 constexpr int kTmaConsumers = 256;
 
-template <int KIND, typename T, bool SMOOTH>
-cudaError_t launch_tma_stat(StatArgs a, cudaStream_t st) {
-  a.tpr = kTmaConsumers;
+template <int KIND, typename T, bool SMOOTH, int VPC>
+cudaError_t launch_tma_stat_v(StatArgs a, cudaStream_t st, int consumers, int stages) {
+  a.tpr = consumers;
   a.rpc = 1;
-  const int block = kTmaConsumers + 32;
-  const size_t smem = RingLayout::total_bytes(kTmaChunk, kTmaStages);
-  const void* fn = reinterpret_cast<const void*>(&tma_stat_kernel<KIND, T, SMOOTH>);
+  const int block = consumers + 32;
+  const size_t smem = RingLayout::total_bytes(kTmaChunk, stages);
+  const void* fn = reinterpret_cast<const void*>(&tma_stat_kernel<KIND, T, SMOOTH, VPC>);
   if (cudaError_t e = allow_dynamic_smem(fn, smem)) return e;
   const int grid = persistent_grid(fn, block, smem, a.M * a.nseg);
-  tma_stat_kernel<KIND, T, SMOOTH><<<grid, block, smem, st>>>(a, kTmaStages, kTmaChunk, kWaitLimitNs);
+  tma_stat_kernel<KIND, T, SMOOTH, VPC><<<grid, block, smem, st>>>(a, stages, kTmaChunk, kWaitLimitNs);
   return cudaGetLastError();
+}
+
+template <int KIND, typename T, bool SMOOTH>
+cudaError_t launch_tma_stat(StatArgs a, cudaStream_t st) {
+  return launch_tma_stat_v<KIND, T, SMOOTH, 4>(a, st, kTmaConsumers, kTmaStages);
 }
 
 template <int KIND, typename T, bool SMOOTH>
@@ -376,7 +399,10 @@ cudaError_t dispatch_vec(StatArgs a, cudaStream_t st) {
   // Explicit selection only: the register kernel is measured faster on B200.
   if (tma_ok && path == DSLPG_PATH_TMA && item_bytes > 0)
     return launch_tma_stat<KIND, T, SMOOTH>(a, st);
-  if (vec && path != DSLPG_PATH_STREAM) return launch_stat<KIND, T, E, SMOOTH>(a, st);
+  // Measured best on B200 for vocab-sized rows: next loads prefetched, one
+  // exponential pair in four on the FMA pipe, registers bounded to three
+  // CTAs per SM.
+  if (vec && path != DSLPG_PATH_STREAM) return launch_stat<KIND, T, E, SMOOTH, 4, true, 4, 3>(a, st);
   return launch_stat<KIND, T, 1, SMOOTH>(a, st);
 }
 
