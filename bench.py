@@ -55,6 +55,29 @@ SHORT = {torch.float32: "fp32", torch.float16: "fp16", torch.bfloat16: "bf16"}
 
 
 # --------------------------------------------------------------------------- env
+_RESULT_FD = None
+
+
+def keep_stdout_for_result():
+    """Send everything written to file descriptor 1 (NCCL banners, library
+    logs) to stderr, keeping a private copy of the real stdout for the one
+    JSON result line."""
+    global _RESULT_FD
+    if _RESULT_FD is None:
+        sys.stdout.flush()
+        _RESULT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, data)
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -416,7 +439,7 @@ def run_reference(args, rank, world):
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -439,12 +462,13 @@ def main(argv=None):
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()
+    keep_stdout_for_result()
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
 
     if not torch.cuda.is_available():
-        print(json.dumps({"error": "no CUDA device"}))
+        emit({"error": "no CUDA device"})
         return 1
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -503,7 +527,7 @@ def main(argv=None):
             "clocks": clocks,
             "kernels": kernels,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
