@@ -264,6 +264,15 @@ def direct_launcher(wl, dev):
             a[0].data_ptr(), a[1].data_ptr(), outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(), M, N, N,
             code, _lib.I64, k["smoothing"], k["logit_scale"], k["lse_square_scale"], k["ignored_index"],
             float(k["total_classes"]), k["class_start_idx"], k["BLOCK_SIZE"], 0, 0, stream)
+    elif cfg.op == "cross_entropy_bwd":
+        k = wl.kwargs
+        dloss, x, lse, labels = a
+        y = torch.empty_like(x)
+        keep = [y]
+        f = lambda: lib.dslpg_cross_entropy_bwd(
+            dloss.data_ptr(), _lib.F32, 1, x.data_ptr(), lse.data_ptr(), labels.data_ptr(), y.data_ptr(), M, N, N, N,
+            code, _lib.I64, k["smoothing"], k["logit_scale"], k["lse_square_scale"], k["ignored_index"],
+            float(k["total_classes"]), k["class_start_idx"], 0, stream)
     else:
         raise KeyError(cfg.op)
 
@@ -291,6 +300,18 @@ def torch_baseline(wl):
         return "torch.logsumexp", lambda: torch.logsumexp(a[0], -1)
     if cfg.op == "cross_entropy":
         return "F.cross_entropy(mean)", lambda: F.cross_entropy(a[0], a[1], ignore_index=-100)
+    if cfg.op == "cross_entropy_bwd":
+        # the vectorised eager form of pytorch_impl.cross_entropy_bwd (its own
+        # Python loop is not a GPU baseline)
+        dloss, x, lse, labels = a
+        keep = labels != -100
+        lab = labels.clamp(min=0)
+
+        def eager():
+            p = torch.exp(x.float() - lse[:, None])
+            p.scatter_add_(1, lab[:, None], -keep[:, None].float())
+            return (p * torch.where(keep, dloss, 0.0)[:, None]).to(x.dtype)
+        return "torch eager dlogits", eager
     raise KeyError(cfg.op)
 
 

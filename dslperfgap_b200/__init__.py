@@ -10,6 +10,6 @@ from .rms_norm.cuda_impl import rms_norm
 from .softmax.cuda_impl import softmax
 from .log_softmax.cuda_impl import log_softmax
 from .logsumexp.cuda_impl import logsumexp
-from .cross_entropy.cuda_impl import cross_entropy_fwd
+from .cross_entropy.cuda_impl import cross_entropy_fwd, cross_entropy_bwd
 
-__all__ = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy_fwd"]
+__all__ = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy_fwd", "cross_entropy_bwd"]

@@ -34,6 +34,10 @@ SIGNATURES = {
         _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
         _c_f32, _c_f32, _c_f32, _c_i64, _c_f32, _c_i64, _c_i64, _c_int, _c_int, _vp,
     ],
+    "dslpg_cross_entropy_bwd": [
+        _vp, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
+        _c_f32, _c_f32, _c_f32, _c_i64, _c_f32, _c_i64, _c_int, _vp,
+    ],
     "dslpg_version": [],
     "dslpg_set_kernel_path": [_c_int],
 }

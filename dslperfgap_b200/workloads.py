@@ -15,6 +15,7 @@ each output written once:
   layer_norm / rms_norm / softmax / log_softmax   2 * M * N * elem_size
   logsumexp                                      M * N * elem_size + M * elem_size
   cross_entropy (one block per row)              M * N * elem_size + 8 * M + 3 * 4 * M
+  cross_entropy_bwd                              2 * M * N * elem_size + 8 * M + 4 * M + 4 * M
 (the [N] weight and bias vectors, read once per GPU, are not counted).
 """
 from __future__ import annotations
@@ -60,6 +61,11 @@ CONFIGS = {
                dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.0, ignored_index=-100,
                     total_classes=128256, class_start_idx=0, BLOCK_SIZE=131072, HAS_SMOOTHING=False,
                     SPLIT=False)),
+        Config("cross_entropy_bwd_bf16", "cross_entropy_bwd", "cross_entropy_bwd", 8192, 128256, torch.bfloat16,
+               "cross-entropy bwd bf16 on the forward's configuration: logits[8192,128256]~N(0,2), int64 targets "
+               "U[0,128256), 410 rows ignore_index=-100, dloss~U(0.5,1.5), lse = row logsumexp",
+               dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.0, ignored_index=-100,
+                    total_classes=128256, class_start_idx=0, BLOCK_SIZE=131072, HAS_SMOOTHING=False)),
         Config("layer_norm_bf16_sharded", "layer_norm", "layer_norm", 131072, 8192, torch.bfloat16,
                "row-sharded LayerNorm bf16 x[131072,8192]~N(0,1), w~N(1,0.1), b~N(0,0.1), eps=1e-5, "
                "row blocks over 1/2/4/8 GPUs", {"eps": 1e-5}),
@@ -121,6 +127,8 @@ def algo_bytes(cfg: Config, rows: int) -> int:
         return rows * cfg.N * es + rows * es
     if cfg.op == "cross_entropy":
         return rows * cfg.N * es + 8 * rows + 3 * 4 * rows
+    if cfg.op == "cross_entropy_bwd":
+        return 2 * rows * cfg.N * es + 8 * rows + 4 * rows + 4 * rows
     raise KeyError(cfg.op)
 
 
@@ -183,13 +191,20 @@ def make(name: str, seed: int = 0, device="cpu", rows: tuple | None = None) -> W
         args = [_rows(cfg, r0, r1, seed, device, 3.0, True)]
     elif cfg.op == "logsumexp":
         args = [_rows(cfg, r0, r1, seed, device, 2.0, False)]
-    elif cfg.op == "cross_entropy":
+    elif cfg.op in ("cross_entropy", "cross_entropy_bwd"):
         x = _rows(cfg, r0, r1, seed, device, 2.0, False)
         g = _gen("cpu", seed + 103)
         labels = torch.randint(0, cfg.N, (cfg.M,), generator=g, dtype=torch.int64)
         n_ign = int(round(0.05 * cfg.M))
         labels[torch.randperm(cfg.M, generator=g)[:n_ign]] = -100
-        args = [x, labels[r0:r1].to(device)]
+        labels = labels[r0:r1].to(device)
+        if cfg.op == "cross_entropy":
+            args = [x, labels]
+        else:
+            dloss = (torch.rand(cfg.M, generator=g) + 0.5)[r0:r1].to(device)
+            # input preparation only: the forward's per-row lse
+            lse = torch.cat([torch.logsumexp(x[i:i + 256].float(), dim=-1) for i in range(0, x.shape[0], 256)])
+            args = [dloss, x, lse, labels]
     else:
         raise KeyError(cfg.op)
     return Workload(cfg, (r0, r1), args, kw)

@@ -149,6 +149,26 @@ DSLPG_API int dslpg_cross_entropy_fwd(const void* logits, const void* labels, fl
                             int64_t block_size, int has_smoothing, int split,
                             cudaStream_t stream);
 
+/*
+ * Blockwise cross-entropy backward: for every row r and column c < n_cols,
+ *   p = exp(logits[r,c] * logit_scale - lse[r]);  p += 2 * lse_square_scale * lse[r] * p;
+ *   p -= (has_smoothing ? 1 - smoothing : 1) at c == labels[r] - class_start_idx;
+ *   p -= smoothing / total_classes                  (has_smoothing only);
+ *   dlogits[r,c] = (dloss[r] * logit_scale) * p, with dloss[r] = 0 where
+ *   labels[r] == ignored_index,
+ * stored in logits_dtype. lse holds one fp32 value per row (the forward's lse
+ * for a single column block); dloss[r] is read at r * dloss_stride.
+ * Replaces cross_entropy_bwd(...) of ViperBench/cross_entropy/pytorch_impl.py:93-141
+ * (kernel: ViperBench/cross_entropy/triton_impl.py:79-120, wrapper :143-158).
+ */
+DSLPG_API int dslpg_cross_entropy_bwd(const void* dloss, int dloss_dtype, int64_t dloss_stride,
+                            const void* logits, const float* lse, const void* labels, void* dlogits,
+                            int64_t n_rows, int64_t n_cols, int64_t logits_row_stride,
+                            int64_t dlogits_row_stride, int logits_dtype, int labels_dtype,
+                            float smoothing, float logit_scale, float lse_square_scale,
+                            int64_t ignored_index, float total_classes, int64_t class_start_idx,
+                            int has_smoothing, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

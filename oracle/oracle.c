@@ -353,6 +353,53 @@ void oracle_cross_entropy_fwd(const void* logits, const void* labels, float* los
   parallel_for(R * a.nb, cross_entropy_items, &a);
 }
 
+/*
+ * cross_entropy_bwd of ViperBench/cross_entropy/pytorch_impl.py:93-141 (the
+ * Triton kernel's arithmetic, triton_impl.py:98-120): for every column,
+ * probs = exp(logits * scale - lse[r]); probs += 2 * lse_sq * lse[r] * probs;
+ * the label column loses (1 - smoothing) (or 1); with smoothing every column
+ * loses smoothing / total_classes; dlogits = (dloss[r] * scale) * probs, with
+ * dloss = 0 on ignored rows. lse[r] and dloss[r] are read at flat index r.
+ */
+typedef struct {
+  const void *dloss, *x, *labels;
+  const float* lse;
+  void* dx;
+  int64_t R, C, ignored, class_start;
+  int ddt, xdt, lbdt, has_smoothing;
+  double smoothing, scale, lse_sq, total_classes;
+} bwd_t;
+
+static void cross_entropy_bwd_rows(const void* ctx, int64_t r0, int64_t r1) {
+  const bwd_t* a = (const bwd_t*)ctx;
+  for (int64_t r = r0; r < r1; ++r) {
+    const int64_t label = a->lbdt == I64 ? ((const int64_t*)a->labels)[r] : (int64_t)((const int32_t*)a->labels)[r];
+    const double dl = label != a->ignored ? load(a->dloss, r, a->ddt) : 0.0;
+    const double lse = (double)a->lse[r];
+    const int64_t adj = label - a->class_start;
+    for (int64_t c = 0; c < a->C; ++c) {
+      double p = exp((double)(float)(load(a->x, r * a->C + c, a->xdt) * a->scale) - lse);
+      p += 2.0 * a->lse_sq * lse * p;
+      if (c == adj) p -= a->has_smoothing ? (1.0 - a->smoothing) : 1.0;
+      if (a->has_smoothing) p -= a->smoothing / a->total_classes;
+      store(a->dx, r * a->C + c, a->xdt, (dl * a->scale) * p);
+    }
+  }
+}
+
+void oracle_cross_entropy_bwd(const void* dloss, int ddt, const void* logits, const float* lse, const void* labels,
+                              void* dlogits, int64_t R, int64_t C, int xdt, int lbdt, double smoothing,
+                              double scale, double lse_sq, int64_t ignored, double total_classes,
+                              int64_t class_start, int has_smoothing) {
+  bwd_t a;
+  memset(&a, 0, sizeof(a));
+  a.dloss = dloss; a.ddt = ddt; a.x = logits; a.lse = lse; a.labels = labels; a.dx = dlogits;
+  a.R = R; a.C = C; a.xdt = xdt; a.lbdt = lbdt; a.smoothing = smoothing; a.scale = scale;
+  a.lse_sq = lse_sq; a.ignored = ignored; a.total_classes = total_classes; a.class_start = class_start;
+  a.has_smoothing = has_smoothing;
+  parallel_for(R, cross_entropy_bwd_rows, &a);
+}
+
 /* Bit-level conversions, exported so tests can check them. */
 float oracle_half_to_float(uint16_t h) { return half_to_float(h); }
 uint16_t oracle_float_to_half(float f) { return float_to_half(f); }

@@ -55,6 +55,8 @@ def lib() -> ctypes.CDLL:
                 l.oracle_logsumexp.argtypes = [vp, vp, i64, i64, ci]
                 l.oracle_cross_entropy_fwd.argtypes = [vp, vp, vp, vp, vp, i64, i64, ci, ci, cd, cd, cd,
                                                        i64, cd, i64, i64, ci, ci, i64]
+                l.oracle_cross_entropy_bwd.argtypes = [vp, ci, vp, vp, vp, vp, i64, i64, ci, ci, cd, cd, cd,
+                                                       i64, cd, i64, ci]
                 l.oracle_set_threads.argtypes = [ci]
                 l.oracle_max_threads.restype = ci
                 l.oracle_half_to_float.argtypes = [ctypes.c_uint16]
@@ -165,3 +167,17 @@ def cross_entropy_fwd(logits, labels, smoothing, logit_scale, lse_square_scale,
         float(lse_square_scale), int(ignored_index), float(total_classes), int(class_start_idx),
         int(BLOCK_SIZE), 1 if HAS_SMOOTHING else 0, 1 if SPLIT else 0, loss.numel())
     return loss, lse, z
+
+
+def cross_entropy_bwd(dloss, logits, lse, labels, smoothing, logit_scale, lse_square_scale,
+                      ignored_index, total_classes, class_start_idx, BLOCK_SIZE, HAS_SMOOTHING):
+    """ViperBench/cross_entropy/pytorch_impl.py:93-141: dlogits with logits' shape and dtype."""
+    dl, lg, lb = _host(dloss), _host(logits), _host(labels)
+    ls = _host(lse).reshape(-1).float().contiguous()
+    r, c = lg.shape
+    dx = torch.empty_like(lg)
+    lib().oracle_cross_entropy_bwd(
+        dl.data_ptr(), _code(dl), lg.data_ptr(), ls.data_ptr(), lb.data_ptr(), dx.data_ptr(), r, c, _code(lg),
+        _LABEL_CODES[lb.dtype], float(smoothing), float(logit_scale), float(lse_square_scale),
+        int(ignored_index), float(total_classes), int(class_start_idx), 1 if HAS_SMOOTHING else 0)
+    return dx

@@ -36,10 +36,11 @@ import torch
 HERE = Path(__file__).resolve().parent
 REF = Path(os.environ.get("DSLPG_REFERENCE", "/root/reference")) / "ViperBench"
 
-OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy"]
+OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd"]
 
 
 def load_ref(kernel: str):
+    kernel = "cross_entropy" if kernel == "cross_entropy_bwd" else kernel
     path = REF / kernel / "pytorch_impl.py"
     spec = importlib.util.spec_from_file_location(f"ref_{kernel}_pytorch_impl", str(path))
     mod = importlib.util.module_from_spec(spec)
@@ -243,7 +244,49 @@ def cases_cross_entropy():
     return c
 
 
+def bwd_case(name, logits, labels, p, seedgen):
+    """cross_entropy_bwd inputs: dloss ~ U(0.5, 1.5) per row and lse = the row's
+    logsumexp of logits * scale (one value per row, as the forward stores it)."""
+    r = logits.shape[0]
+    dloss = torch.rand(r, generator=seedgen) + 0.5
+    lse = torch.logsumexp(logits.float() * p["logit_scale"], dim=-1)
+    kw = {k: v for k, v in p.items() if k != "SPLIT"}
+    return (name, [dloss, logits, lse, labels], kw)
+
+
+def cases_cross_entropy_bwd():
+    c = []
+    g42 = torch.Generator().manual_seed(42)  # the reference test's seed (test.py:13-17), CPU generator
+    logits = torch.randn((4, 8), generator=g42, dtype=torch.float32)
+    labels = torch.randint(0, 8, (4,), generator=g42, dtype=torch.int32)
+    for name, p in CE_REF_CONFIGS:
+        c.append(bwd_case(f"ref_{name}", logits, labels, dict(p), GEN))
+    lg = randn(2, 128256, std=2.0, dtype=torch.bfloat16)
+    lb = torch.tensor([5, 128255], dtype=torch.int64)
+    c.append(bwd_case("cfg_bf16_vocab", lg, lb, dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.0,
+                                                      ignored_index=-100, total_classes=128256, class_start_idx=0,
+                                                      BLOCK_SIZE=131072, HAS_SMOOTHING=False, SPLIT=False), GEN))
+    lg2 = randn(6, 1000, dtype=torch.bfloat16)
+    lb2 = torch.tensor([999, -100, 3, 500, 0, 1500], dtype=torch.int64)
+    c.append(bwd_case("multiblock_smooth_scale", lg2, lb2, dict(smoothing=0.2, logit_scale=0.7, lse_square_scale=1e-3,
+                                                                ignored_index=-100, total_classes=1000, class_start_idx=0,
+                                                                BLOCK_SIZE=256, HAS_SMOOTHING=True, SPLIT=False), GEN))
+    lg3 = randn(5, 96, dtype=torch.float16)
+    lb3 = torch.tensor([45, 200, 100, -7, 50], dtype=torch.int32)
+    c.append(bwd_case("class_start_fp16", lg3, lb3, dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.01,
+                                                         ignored_index=-7, total_classes=96, class_start_idx=40,
+                                                         BLOCK_SIZE=64, HAS_SMOOTHING=False, SPLIT=False), GEN))
+    lg4 = randn(3, 37)
+    lb4 = torch.tensor([0, 36, 12], dtype=torch.int64)
+    c.append(bwd_case("odd_cols_fp32", lg4, lb4, dict(smoothing=0.1, logit_scale=2.0, lse_square_scale=0.0,
+                                                      ignored_index=-100, total_classes=37, class_start_idx=0,
+                                                      BLOCK_SIZE=16, HAS_SMOOTHING=True, SPLIT=False), GEN))
+    return c
+
+
 def call(op, mod, args, kwargs):
+    if op == "cross_entropy_bwd":
+        return mod.cross_entropy_bwd(*args, **kwargs)
     if op == "layer_norm":
         return mod.layer_norm(*args, **kwargs)
     if op == "rms_norm":
@@ -269,7 +312,8 @@ def valid_prefix(outs, n_rows, n_cols, bs):
 
 def main() -> int:
     builders = dict(layer_norm=cases_layer_norm, rms_norm=cases_rms_norm, softmax=cases_softmax,
-                    log_softmax=cases_log_softmax, logsumexp=cases_logsumexp, cross_entropy=cases_cross_entropy)
+                    log_softmax=cases_log_softmax, logsumexp=cases_logsumexp, cross_entropy=cases_cross_entropy,
+                    cross_entropy_bwd=cases_cross_entropy_bwd)
     total = 0
     for op in OPS:
         mod = load_ref(op)

@@ -6,7 +6,7 @@ from pathlib import Path
 import torch
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy"]
+OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd"]
 _cache: dict = {}
 
 
@@ -27,7 +27,8 @@ def ids():
 
 
 FN_NAME = {"layer_norm": "layer_norm", "rms_norm": "rms_norm", "softmax": "softmax",
-           "log_softmax": "log_softmax", "logsumexp": "logsumexp", "cross_entropy": "cross_entropy_fwd"}
+           "log_softmax": "log_softmax", "logsumexp": "logsumexp", "cross_entropy": "cross_entropy_fwd",
+           "cross_entropy_bwd": "cross_entropy_bwd"}
 
 
 def run(fn, op: str, case: dict, device: str = "cpu"):

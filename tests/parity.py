@@ -90,6 +90,8 @@ def out_dtype(op: str, args, kwargs) -> torch.dtype:
         return getattr(torch, kwargs["dtype"])
     if op == "cross_entropy":
         return torch.float32
+    if op == "cross_entropy_bwd":
+        return args[1].dtype
     return args[0].dtype
 
 

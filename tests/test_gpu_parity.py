@@ -290,3 +290,39 @@ def test_no_pipeline_wait_ran_out():
     """Run last in this file: no bounded device wait expired in any test above."""
     torch.cuda.synchronize()
     assert _lib.take_wait_timeouts() == 0
+
+
+# ---------------------------------------------------------- cross_entropy_bwd
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("n", [8, 37, 1000, 4096, 40000, 128256])
+@pytest.mark.parametrize("smooth", [False, True])
+def test_cross_entropy_bwd(n, dt, smooth):
+    g = gen(n + 17)
+    r = 12
+    lg = randn((r, n), DT[dt], g, std=2.0)
+    lb = torch.randint(0, n, (r,), generator=g, dtype=torch.int64)
+    lb[1] = -100
+    lb[2] = n + 3          # in no column
+    lb[3] = n - 1          # last column
+    lb[4] = 0
+    dloss = torch.rand(r, generator=g) + 0.5
+    lse = torch.logsumexp(lg.float() * 0.8, dim=-1)
+    kw = dict(smoothing=0.1 if smooth else 0.0, logit_scale=0.8, lse_square_scale=1e-3, ignored_index=-100,
+              total_classes=n, class_start_idx=0, BLOCK_SIZE=4096, HAS_SMOOTHING=smooth)
+    out = B.cross_entropy_bwd(dloss.cuda(), lg.cuda(), lse.cuda(), lb.cuda(), **kw)
+    assert out.dtype == DT[dt] and out.shape == lg.shape
+    assert_parity(out, oracle.cross_entropy_bwd(dloss, lg, lse, lb, **kw), DT[dt])
+
+
+def test_cross_entropy_bwd_strided_and_int32_labels():
+    g = gen(99)
+    full = randn((6, 3000), torch.bfloat16, g)
+    lb = torch.tensor([5, 2499, -100, 0, 7, 100], dtype=torch.int32)
+    dloss_full = torch.rand(12, generator=g) + 0.5
+    dloss = dloss_full[::2]  # stride 2
+    lse = torch.logsumexp(full[:, :2500].float(), dim=-1)
+    kw = dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.0, ignored_index=-100, total_classes=2500,
+              class_start_idx=2, BLOCK_SIZE=1024, HAS_SMOOTHING=False)
+    out = B.cross_entropy_bwd(dloss_full.cuda()[::2], full.cuda()[:, :2500], lse.cuda(), lb.cuda(), **kw)
+    ref = oracle.cross_entropy_bwd(dloss.contiguous(), full[:, :2500].contiguous(), lse, lb, **kw)
+    assert_parity(out, ref, torch.bfloat16)
