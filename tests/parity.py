@@ -5,6 +5,10 @@
   reference value; normalised outputs (layer_norm, rms_norm) may also pass
   with |out - ref| <= 2e-2.
 * NaN and +/-inf must appear at exactly the reference's positions.
+* `abs_slack` (optional, per element or scalar) widens the bound where the
+  reference itself subtracts nearly equal fp32 terms (cross_entropy_bwd with
+  smoothing: p - smoothing/total_classes): there any fp32 implementation
+  differs by the fp32 rounding of the terms, 2^-21 of their magnitude.
 The reference's own check (ViperBench/test_utils.py:11-35, loose=True: fp32
 2e-5, fp16 2e-3, bf16 2e-2, atol = rtol) is `reference_allclose`.
 """
@@ -29,7 +33,7 @@ def dtype_ulp(ref: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
 
 
 def compare(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, normalised: bool = False,
-            chunk: int = 1 << 24):
+            chunk: int = 1 << 24, abs_slack=None):
     """Return (ok, message) for the parity rule above (checked in chunks)."""
     out = out.detach().reshape(-1)
     ref = ref.detach().reshape(-1)
@@ -37,8 +41,12 @@ def compare(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, normalised
         return False, f"shape {tuple(out.shape)} != {tuple(ref.shape)}"
     worst = 0.0
     for s in range(0, max(out.numel(), 1), chunk):
+        sl = None
+        if abs_slack is not None:
+            sl = (abs_slack.reshape(-1)[s:s + chunk].cpu().double() if isinstance(abs_slack, torch.Tensor)
+                  else float(abs_slack))
         ok, msg, w = _compare_chunk(out[s:s + chunk].cpu().double(), ref[s:s + chunk].cpu().double(), dtype,
-                                    normalised, s)
+                                    normalised, s, sl)
         if not ok:
             return False, msg
         worst = max(worst, w)
@@ -47,7 +55,7 @@ def compare(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, normalised
     return True, f"max ulps={worst:.3f}"
 
 
-def _compare_chunk(out, ref, dtype, normalised, offset):
+def _compare_chunk(out, ref, dtype, normalised, offset, slack=None):
     on, rn = torch.isnan(out), torch.isnan(ref)
     if not torch.equal(on, rn):
         return False, f"NaN pattern differs ({int(on.sum())} vs {int(rn.sum())} NaNs)", 0.0
@@ -56,11 +64,16 @@ def _compare_chunk(out, ref, dtype, normalised, offset):
         return False, "inf pattern differs", 0.0
     fin = ~(rn | ri)
     o, r = out[fin], ref[fin]
+    if isinstance(slack, torch.Tensor):
+        slack = slack[fin]
     if o.numel() == 0:
         return True, "", 0.0
     d = (o - r).abs()
     if dtype == torch.float32:
-        bad = d > FP32_TOL + FP32_TOL * r.abs()
+        bound = FP32_TOL + FP32_TOL * r.abs()
+        if slack is not None:
+            bound = bound + slack
+        bad = d > bound
         what = "atol=rtol=1e-5"
         worst = d.max().item()
     else:
@@ -68,6 +81,8 @@ def _compare_chunk(out, ref, dtype, normalised, offset):
         bound = u * (1 + 1e-9)
         if normalised:
             bound = torch.maximum(bound, torch.full_like(bound, NORM_ATOL_16))
+        if slack is not None:
+            bound = bound + slack
         bad = d > bound
         what = "1 ulp" + (" or 2e-2" if normalised else "")
         worst = (d / u).max().item()
