@@ -264,6 +264,17 @@ def direct_launcher(wl, dev):
             a[0].data_ptr(), a[1].data_ptr(), outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(), M, N, N,
             code, _lib.I64, k["smoothing"], k["logit_scale"], k["lse_square_scale"], k["ignored_index"],
             float(k["total_classes"]), k["class_start_idx"], k["BLOCK_SIZE"], 0, 0, stream)
+    elif cfg.op in ("mean_reduction", "max_reduction", "argmax"):
+        x = a[0]
+        vals = torch.empty(M, dtype=cfg.dtype, device=dev)
+        idx = torch.empty(M, dtype=torch.int64, device=dev)
+        keep = [vals, idx]
+        if cfg.op == "mean_reduction":
+            f = lambda: lib.dslpg_mean_reduction(x.data_ptr(), vals.data_ptr(), M, N, 1, code, code, stream)
+        elif cfg.op == "max_reduction":
+            f = lambda: lib.dslpg_max_reduction(x.data_ptr(), vals.data_ptr(), idx.data_ptr(), M, N, 1, code, stream)
+        else:
+            f = lambda: lib.dslpg_argmax(x.data_ptr(), idx.data_ptr(), M, N, 1, code, stream)
     elif cfg.op == "cross_entropy_bwd":
         k = wl.kwargs
         dloss, x, lse, labels = a
@@ -300,6 +311,12 @@ def torch_baseline(wl):
         return "torch.logsumexp", lambda: torch.logsumexp(a[0], -1)
     if cfg.op == "cross_entropy":
         return "F.cross_entropy(mean)", lambda: F.cross_entropy(a[0], a[1], ignore_index=-100)
+    if cfg.op == "mean_reduction":
+        return "torch.mean", lambda: torch.mean(a[0], 1)
+    if cfg.op == "max_reduction":
+        return "torch.max(dim)", lambda: torch.max(a[0], 1)
+    if cfg.op == "argmax":
+        return "torch.argmax", lambda: torch.argmax(a[0], 1)
     if cfg.op == "cross_entropy_bwd":
         # the vectorised eager form of pytorch_impl.cross_entropy_bwd (its own
         # Python loop is not a GPU baseline)

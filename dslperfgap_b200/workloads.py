@@ -16,6 +16,7 @@ each output written once:
   logsumexp                                      M * N * elem_size + M * elem_size
   cross_entropy (one block per row)              M * N * elem_size + 8 * M + 3 * 4 * M
   cross_entropy_bwd                              2 * M * N * elem_size + 8 * M + 4 * M + 4 * M
+  mean_reduction / max_reduction / argmax        M * N * elem_size + the M outputs
 (the [N] weight and bias vectors, read once per GPU, are not counted).
 """
 from __future__ import annotations
@@ -66,6 +67,13 @@ CONFIGS = {
                "U[0,128256), 410 rows ignore_index=-100, dloss~U(0.5,1.5), lse = row logsumexp",
                dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.0, ignored_index=-100,
                     total_classes=128256, class_start_idx=0, BLOCK_SIZE=131072, HAS_SMOOTHING=False)),
+        Config("mean_reduction_fp32", "mean_reduction", "mean_reduction", 8192, 32768, torch.float32,
+               "mean over dim 1, fp32 x[8192,32768]~N(0,1) (the reference's large shape, benchmark.py:288-290)",
+               {"dim": 1}),
+        Config("max_reduction_fp16", "max_reduction", "max_reduction", 8192, 32768, torch.float16,
+               "max (values, indices) over dim 1, fp16 x[8192,32768]~N(0,1) (benchmark.py:278-280)", {"dim": 1}),
+        Config("argmax_fp16", "argmax", "argmax", 8192, 32768, torch.float16,
+               "argmax over dim 1, fp16 x[8192,32768]~N(0,1) (benchmark.py:97-99)", {"dim": 1}),
         Config("layer_norm_bf16_sharded", "layer_norm", "layer_norm", 131072, 8192, torch.bfloat16,
                "row-sharded LayerNorm bf16 x[131072,8192]~N(0,1), w~N(1,0.1), b~N(0,0.1), eps=1e-5, "
                "row blocks over 1/2/4/8 GPUs", {"eps": 1e-5}),
@@ -99,7 +107,11 @@ class Workload:
 
     @property
     def out_dtype(self):
-        return torch.float32 if self.op == "cross_entropy" else self.config.dtype
+        if self.op == "cross_entropy":
+            return torch.float32
+        if self.op == "argmax":
+            return torch.int64
+        return self.config.dtype
 
     @property
     def cuda_fn(self):
@@ -129,6 +141,12 @@ def algo_bytes(cfg: Config, rows: int) -> int:
         return rows * cfg.N * es + 8 * rows + 3 * 4 * rows
     if cfg.op == "cross_entropy_bwd":
         return 2 * rows * cfg.N * es + 8 * rows + 4 * rows + 4 * rows
+    if cfg.op == "mean_reduction":
+        return rows * cfg.N * es + rows * es
+    if cfg.op == "max_reduction":
+        return rows * cfg.N * es + rows * (es + 8)
+    if cfg.op == "argmax":
+        return rows * cfg.N * es + rows * 8
     raise KeyError(cfg.op)
 
 
@@ -191,6 +209,8 @@ def make(name: str, seed: int = 0, device="cpu", rows: tuple | None = None) -> W
         args = [_rows(cfg, r0, r1, seed, device, 3.0, True)]
     elif cfg.op == "logsumexp":
         args = [_rows(cfg, r0, r1, seed, device, 2.0, False)]
+    elif cfg.op in ("mean_reduction", "max_reduction", "argmax"):
+        args = [_rows(cfg, r0, r1, seed, device, 1.0, False)]
     elif cfg.op in ("cross_entropy", "cross_entropy_bwd"):
         x = _rows(cfg, r0, r1, seed, device, 2.0, False)
         g = _gen("cpu", seed + 103)

@@ -169,6 +169,30 @@ DSLPG_API int dslpg_cross_entropy_bwd(const void* dloss, int dloss_dtype, int64_
                             int64_t ignored_index, float total_classes, int64_t class_start_idx,
                             int has_smoothing, cudaStream_t stream);
 
+/*
+ * Reductions over the middle axis of a dense [M, N, K] tensor (a reduced run
+ * of adjacent axes is one N; K == 1 reduces rows). Index outputs are int64 and
+ * follow torch: the first NaN is the maximum; equal maxima give the smallest
+ * index.
+ *
+ * mean: y[M*K] of out_dtype = sum / N, accumulated in fp32 after converting x
+ * to out_dtype (torch.mean(x, dim, dtype=out_dtype)).
+ * Replaces mean_reduction(input_tensor, dim, keepdim, dtype) of
+ * ViperBench/mean_reduction/pytorch_impl.py:4-8.
+ */
+DSLPG_API int dslpg_mean_reduction(const void* x, void* y, int64_t M, int64_t N, int64_t K, int in_dtype,
+                                   int out_dtype, cudaStream_t stream);
+
+/* values[M*K] (x's dtype) and indices[M*K] of the maximum along N.
+ * Replaces max_reduction(input, dim, keepdim) of ViperBench/max_reduction/pytorch_impl.py:4-11. */
+DSLPG_API int dslpg_max_reduction(const void* x, void* values, int64_t* indices, int64_t M, int64_t N,
+                                  int64_t K, int dtype, cudaStream_t stream);
+
+/* indices[M*K] of the maximum along N.
+ * Replaces argmax(input_tensor, dim, keepdim) of ViperBench/argmax/pytorch_impl.py:4-8. */
+DSLPG_API int dslpg_argmax(const void* x, int64_t* indices, int64_t M, int64_t N, int64_t K, int dtype,
+                           cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -400,6 +400,62 @@ void oracle_cross_entropy_bwd(const void* dloss, int ddt, const void* logits, co
   parallel_for(R, cross_entropy_bwd_rows, &a);
 }
 
+/*
+ * Reductions over the middle axis of [M, N, K]:
+ *   mean   torch.mean(x, dim, dtype=odt)  (ViperBench/mean_reduction/pytorch_impl.py:4-8):
+ *          x converted to odt, summed (double here), divided by N;
+ *   max    torch.max(x, dim)               (ViperBench/max_reduction/pytorch_impl.py:4-11)
+ *   argmax torch.argmax(x, dim)            (ViperBench/argmax/pytorch_impl.py:4-8):
+ *          the first NaN is the maximum; equal maxima give the first index.
+ */
+typedef struct {
+  const void* x;
+  void* y;
+  int64_t* idx;
+  int64_t M, N, K;
+  int idt, odt, want_vals;
+} red_t;
+
+static void mean_cols(const void* ctx, int64_t c0, int64_t c1) {
+  const red_t* a = (const red_t*)ctx;
+  for (int64_t c = c0; c < c1; ++c) {
+    const int64_t mi = c / a->K, k = c % a->K, o = mi * a->N * a->K + k;
+    double s = 0.0;
+    for (int64_t n = 0; n < a->N; ++n) s += round_to(load(a->x, o + n * a->K, a->idt), a->odt);
+    store(a->y, c, a->odt, s / (double)a->N);
+  }
+}
+
+static void max_cols(const void* ctx, int64_t c0, int64_t c1) {
+  const red_t* a = (const red_t*)ctx;
+  for (int64_t c = c0; c < c1; ++c) {
+    const int64_t mi = c / a->K, k = c % a->K, o = mi * a->N * a->K + k;
+    double best = load(a->x, o, a->idt);
+    int64_t bi = 0;
+    for (int64_t n = 1; n < a->N && !isnan(best); ++n) {
+      const double v = load(a->x, o + n * a->K, a->idt);
+      if (isnan(v) || v > best) { best = v; bi = n; }
+    }
+    if (a->want_vals) store(a->y, c, a->idt, best);
+    a->idx[c] = bi;
+  }
+}
+
+void oracle_mean_reduction(const void* x, void* y, int64_t M, int64_t N, int64_t K, int idt, int odt) {
+  red_t a;
+  memset(&a, 0, sizeof(a));
+  a.x = x; a.y = y; a.M = M; a.N = N; a.K = K; a.idt = idt; a.odt = odt;
+  parallel_for(M * K, mean_cols, &a);
+}
+
+void oracle_max_reduction(const void* x, void* values, int64_t* indices, int64_t M, int64_t N, int64_t K,
+                          int dt) {
+  red_t a;
+  memset(&a, 0, sizeof(a));
+  a.x = x; a.y = values; a.idx = indices; a.M = M; a.N = N; a.K = K; a.idt = dt; a.want_vals = values != 0;
+  parallel_for(M * K, max_cols, &a);
+}
+
 /* Bit-level conversions, exported so tests can check them. */
 float oracle_half_to_float(uint16_t h) { return half_to_float(h); }
 uint16_t oracle_float_to_half(float f) { return float_to_half(f); }

@@ -57,6 +57,8 @@ def lib() -> ctypes.CDLL:
                                                        i64, cd, i64, i64, ci, ci, i64]
                 l.oracle_cross_entropy_bwd.argtypes = [vp, ci, vp, vp, vp, vp, i64, i64, ci, ci, cd, cd, cd,
                                                        i64, cd, i64, ci]
+                l.oracle_mean_reduction.argtypes = [vp, vp, i64, i64, i64, ci, ci]
+                l.oracle_max_reduction.argtypes = [vp, vp, vp, i64, i64, i64, ci]
                 l.oracle_set_threads.argtypes = [ci]
                 l.oracle_max_threads.restype = ci
                 l.oracle_half_to_float.argtypes = [ctypes.c_uint16]
@@ -181,3 +183,66 @@ def cross_entropy_bwd(dloss, logits, lse, labels, smoothing, logit_scale, lse_sq
         _LABEL_CODES[lb.dtype], float(smoothing), float(logit_scale), float(lse_square_scale),
         int(ignored_index), float(total_classes), int(class_start_idx), 1 if HAS_SMOOTHING else 0)
     return dx
+
+
+def _mnk(x, dims):
+    """(contiguous x, M, N, K, output shape without keepdim) for reducing `dims`."""
+    shape = tuple(x.shape) if x.dim() else (1,)
+    nd = len(shape)
+    dims = sorted(d % nd for d in ([dims] if isinstance(dims, int) else dims))
+    keep = [d for d in range(nd) if d not in dims]
+    if dims == list(range(dims[0], dims[-1] + 1)):
+        m = math.prod(shape[:dims[0]])
+        n = math.prod(shape[dims[0]:dims[-1] + 1])
+        k = math.prod(shape[dims[-1] + 1:])
+        xc = x.reshape(shape).contiguous()
+    else:
+        xc = x.reshape(shape).permute(*keep, *dims).contiguous()
+        m, n, k = math.prod(shape[d] for d in keep), math.prod(shape[d] for d in dims), 1
+    return xc, m, n, k, dims, shape
+
+
+def _oshape(shape, dims, keepdim, scalar):
+    if scalar:
+        return ()
+    if keepdim:
+        return tuple(1 if i in dims else s for i, s in enumerate(shape))
+    return tuple(s for i, s in enumerate(shape) if i not in dims)
+
+
+def mean_reduction(input_tensor, dim, keepdim=False, dtype=None):
+    """torch.mean(x, dim, keepdim, dtype); ViperBench/mean_reduction/pytorch_impl.py:4-8."""
+    x = _host(input_tensor)
+    odt = x.dtype if dtype is None else dtype
+    xc, m, n, k, dims, shape = _mnk(x, dim)
+    y = torch.empty(_oshape(shape, dims, keepdim, x.dim() == 0), dtype=odt)
+    lib().oracle_mean_reduction(xc.data_ptr(), y.data_ptr(), m, n, k, _code(x), _CODES[odt])
+    return y
+
+
+def max_reduction(input, dim, keepdim=False):
+    """torch.max(x, dim, keepdim) -> (values, indices); ViperBench/max_reduction/pytorch_impl.py:4-11."""
+    if not isinstance(input, torch.Tensor):
+        raise TypeError('The input must be a torch.Tensor.')
+    x = _host(input)
+    xc, m, n, k, dims, shape = _mnk(x, dim)
+    os_ = _oshape(shape, dims, keepdim, x.dim() == 0)
+    v = torch.empty(os_, dtype=x.dtype)
+    i = torch.empty(os_, dtype=torch.int64)
+    lib().oracle_max_reduction(xc.data_ptr(), v.data_ptr(), i.data_ptr(), m, n, k, _code(x))
+    return (v, i)
+
+
+def argmax(input_tensor, dim, keepdim=False):
+    """torch.argmax(x, dim, keepdim); ViperBench/argmax/pytorch_impl.py:4-8."""
+    x = _host(input_tensor)
+    if dim is None:
+        shape = tuple(x.shape)
+        xc, m, n, k = x.reshape(-1).contiguous(), 1, x.numel(), 1
+        os_ = tuple(1 for _ in shape) if keepdim else ()
+    else:
+        xc, m, n, k, dims, shape = _mnk(x, dim)
+        os_ = _oshape(shape, dims, keepdim, x.dim() == 0)
+    i = torch.empty(os_, dtype=torch.int64)
+    lib().oracle_max_reduction(xc.data_ptr(), None, i.data_ptr(), m, n, k, _code(x))
+    return i

@@ -36,7 +36,8 @@ import torch
 HERE = Path(__file__).resolve().parent
 REF = Path(os.environ.get("DSLPG_REFERENCE", "/root/reference")) / "ViperBench"
 
-OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd"]
+OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd",
+       "mean_reduction", "max_reduction", "argmax"]
 
 
 def load_ref(kernel: str):
@@ -284,7 +285,59 @@ def cases_cross_entropy_bwd():
     return c
 
 
+def cases_mean_reduction():
+    c = []
+    for name, shape, dim, kw in [("ref_2D_dim0", (64, 128), 0, {}), ("ref_2D_dim1_keepdim", (64, 128), 1, {"keepdim": True}),
+                                 ("ref_4D_multi_dim", (2, 3, 4, 5), [1, 2], {}), ("ref_3D_dim2", (8, 16, 32), 2, {})]:
+        c.append((name, [randn(*shape), dim], kw))
+    c.append(("cfg_fp32_32768", [randn(4, 32768), 1], {}))
+    c.append(("bf16_dtype_fp32", [randn(8, 1000, dtype=torch.bfloat16), 1], {"dtype": "float32"}))
+    c.append(("fp16_rows", [randn(8, 4096, dtype=torch.float16), -1], {}))
+    c.append(("fp32_to_bf16", [randn(4, 256), 1], {"dtype": "bfloat16"}))
+    c.append(("non_adjacent_dims", [randn(3, 4, 5, 6), [0, 2]], {}))
+    c.append(("odd_3x33", [randn(3, 33), 1], {}))
+    for k in ["nan", "posinf", "large_mag", "all_equal_rows"]:
+        c.append((f"edge_{k}", [edge(k, (4, 64), torch.float32), 1], {}))
+    return c
+
+
+def _argmax_inputs():
+    c = []
+    for name, shape, dim, kw in [("ref_2D_dim0", (128, 256), 0, {}), ("ref_2D_dim1", (256, 128), 1, {}),
+                                 ("ref_3D_dim2", (8, 16, 128), 2, {}), ("ref_3D_dim1_keepdim", (4, 32, 64), 1, {"keepdim": True}),
+                                 ("ref_3D_neg_dim", (4, 8, 64), -1, {})]:
+        c.append((name, [randn(*shape), dim], kw))
+    c.append(("cfg_fp16_32768", [randn(4, 32768, dtype=torch.float16), 1], {}))
+    c.append(("bf16_1000", [randn(6, 1000, dtype=torch.bfloat16), 1], {}))
+    ties = torch.zeros(4, 96)
+    ties[0, 10] = ties[0, 50] = 3.0
+    ties[1] = 1.0
+    ties[2, 95] = 7.0
+    ties[3, :] = float("-inf")
+    c.append(("ties_and_neginf", [ties, 1], {}))
+    nanrow = randn(3, 80)
+    nanrow[0, 7] = float("nan")
+    nanrow[0, 40] = float("nan")
+    nanrow[1, 79] = float("nan")
+    c.append(("nans_first_wins", [nanrow, 1], {}))
+    c.append(("odd_5x33_fp16", [randn(5, 33, dtype=torch.float16), 1], {}))
+    return c
+
+
+def cases_max_reduction():
+    return _argmax_inputs()
+
+
+def cases_argmax():
+    return _argmax_inputs()
+
+
 def call(op, mod, args, kwargs):
+    if op in ("mean_reduction", "max_reduction", "argmax"):
+        kw = dict(kwargs)
+        if "dtype" in kw:
+            kw["dtype"] = getattr(torch, kw["dtype"])
+        return getattr(mod, op)(*args, **kw)
     if op == "cross_entropy_bwd":
         return mod.cross_entropy_bwd(*args, **kwargs)
     if op == "layer_norm":
@@ -313,14 +366,18 @@ def valid_prefix(outs, n_rows, n_cols, bs):
 def main() -> int:
     builders = dict(layer_norm=cases_layer_norm, rms_norm=cases_rms_norm, softmax=cases_softmax,
                     log_softmax=cases_log_softmax, logsumexp=cases_logsumexp, cross_entropy=cases_cross_entropy,
-                    cross_entropy_bwd=cases_cross_entropy_bwd)
+                    cross_entropy_bwd=cases_cross_entropy_bwd, mean_reduction=cases_mean_reduction,
+                    max_reduction=cases_max_reduction, argmax=cases_argmax)
     total = 0
     for op in OPS:
         mod = load_ref(op)
         out = []
         for name, args, kwargs in builders[op]():
             native = call(op, mod, args, kwargs)
-            if op == "log_softmax" and "dtype" in kwargs:
+            if op == "mean_reduction" and "dtype" in kwargs:
+                x32 = args[0].to(getattr(torch, kwargs["dtype"])).float()
+                ref32 = call(op, mod, [x32, args[1]], {k: v for k, v in kwargs.items() if k != "dtype"})
+            elif op == "log_softmax" and "dtype" in kwargs:
                 x32 = args[0].to(getattr(torch, kwargs["dtype"])).float()
                 ref32 = call(op, mod, [x32], {"dim": kwargs.get("dim", -1)})
             else:
@@ -331,7 +388,8 @@ def main() -> int:
                 ref32 = valid_prefix(ref32, r, cc, kwargs["BLOCK_SIZE"])
             out.append(dict(name=name, args=args, kwargs=kwargs, ref_f32=ref32, ref_native=native))
         path = HERE / f"golden_{op}.pt"
-        torch.save(dict(op=op, source="ViperBench/%s/pytorch_impl.py (reference, CPU)" % op,
+        src = "cross_entropy" if op == "cross_entropy_bwd" else op
+        torch.save(dict(op=op, source="ViperBench/%s/pytorch_impl.py (reference, CPU)" % src,
                         torch=str(torch.__version__), cases=out), path)
         total += path.stat().st_size
         print(f"{path.name}: {len(out)} cases, {path.stat().st_size / 1e6:.2f} MB")

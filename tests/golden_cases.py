@@ -6,7 +6,8 @@ from pathlib import Path
 import torch
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd"]
+OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd",
+       "mean_reduction", "max_reduction", "argmax"]
 _cache: dict = {}
 
 
@@ -28,7 +29,8 @@ def ids():
 
 FN_NAME = {"layer_norm": "layer_norm", "rms_norm": "rms_norm", "softmax": "softmax",
            "log_softmax": "log_softmax", "logsumexp": "logsumexp", "cross_entropy": "cross_entropy_fwd",
-           "cross_entropy_bwd": "cross_entropy_bwd"}
+           "cross_entropy_bwd": "cross_entropy_bwd", "mean_reduction": "mean_reduction",
+           "max_reduction": "max_reduction", "argmax": "argmax"}
 
 
 def run(fn, op: str, case: dict, device: str = "cpu"):
@@ -39,27 +41,30 @@ def run(fn, op: str, case: dict, device: str = "cpu"):
         return a.to(device) if isinstance(a, torch.Tensor) else a
     args = [mv(a) for a in case["args"]]
     kw = dict(case["kwargs"])
-    if op == "log_softmax" and "dtype" in kw:
+    if op in ("log_softmax", "mean_reduction") and "dtype" in kw:
         kw["dtype"] = getattr(torch, kw["dtype"])
     out = fn(*args, **kw)
+    if isinstance(out, tuple):
+        out = tuple(o.cpu() for o in out)
     if op == "cross_entropy":
         r, c = case["args"][0].shape
         nb = (c + kw["BLOCK_SIZE"] - 1) // kw["BLOCK_SIZE"]
         return tuple(o.reshape(-1)[: nb * r].cpu() for o in out)
-    return out.cpu()
+    return out if isinstance(out, tuple) else out.cpu()
 
 
 def check_case(op: str, case: dict, out, parity) -> list[str]:
     """Compare an implementation's output with the fixture; return failures."""
     errs = []
-    refs32 = case["ref_f32"] if op == "cross_entropy" else (case["ref_f32"],)
-    natives = case["ref_native"] if op == "cross_entropy" else (case["ref_native"],)
-    outs = out if op == "cross_entropy" else (out,)
+    multi = isinstance(case["ref_native"], tuple)
+    refs32 = case["ref_f32"] if multi else (case["ref_f32"],)
+    natives = case["ref_native"] if multi else (case["ref_native"],)
+    outs = out if multi else (out,)
     split = op == "cross_entropy" and case["kwargs"]["SPLIT"]
     for i, (o, r32, rn) in enumerate(zip(outs, refs32, natives)):
         if split and i == 2:  # z_loss is not stored under SPLIT (cross_entropy/test.py:40-44)
             continue
-        dt = parity.out_dtype(op, case["args"], case["kwargs"])
+        dt = rn.dtype  # the reference's own output dtype
         if o.dtype != rn.dtype or tuple(o.shape) != tuple(rn.shape):
             errs.append(f"output {i}: dtype/shape {o.dtype}{tuple(o.shape)} != {rn.dtype}{tuple(rn.shape)}")
             continue

@@ -39,6 +39,9 @@ def compare(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype, normalised
     ref = ref.detach().reshape(-1)
     if out.shape != ref.shape:
         return False, f"shape {tuple(out.shape)} != {tuple(ref.shape)}"
+    if not dtype.is_floating_point:  # indices: exact
+        eq = torch.equal(out.cpu(), ref.cpu().to(out.dtype))
+        return eq, "exact" if eq else f"{int((out.cpu() != ref.cpu()).sum())} indices differ"
     worst = 0.0
     for s in range(0, max(out.numel(), 1), chunk):
         sl = None
@@ -95,6 +98,8 @@ def _compare_chunk(out, ref, dtype, normalised, offset, slack=None):
 
 def reference_allclose(out: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype) -> bool:
     """ViperBench/test_utils.py:21-35 with loose=True, NaN positions compared equal."""
+    if not dtype.is_floating_point:
+        return torch.equal(out.cpu(), ref.cpu())
     tol = 2 * _REF_TOL.get(dtype, 1e-5)
     return bool(torch.allclose(ref.detach().cpu().float(), out.detach().cpu().float(),
                                atol=tol, rtol=tol, equal_nan=True))

@@ -332,3 +332,58 @@ def test_cross_entropy_bwd_strided_and_int32_labels():
     out = B.cross_entropy_bwd(dloss_full.cuda()[::2], full.cuda()[:, :2500], lse.cuda(), lb.cuda(), **kw)
     ref = oracle.cross_entropy_bwd(dloss.contiguous(), full[:, :2500].contiguous(), lse, lb, **kw)
     assert_parity(out, ref, torch.bfloat16)
+
+
+# --------------------------------------------- mean_reduction / max / argmax
+RED_LENGTHS = [1, 7, 33, 64, 1000, 4096, 32768, 100000]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("n", RED_LENGTHS)
+def test_reductions_rows(n, dt):
+    g = gen(n + 31)
+    x = randn((rows_for(n), n), DT[dt], g)
+    if n >= 8:
+        x[0, n // 3] = float("nan")
+        x[0, n // 2] = float("nan")
+        x[1, :] = 1.0                 # all ties: index 0
+        x[2, n - 1] = 100.0           # maximum in the last column
+        x[3, :] = float("-inf")
+    xc = x.cuda()
+    assert_parity(B.mean_reduction(xc, 1), oracle.mean_reduction(x, 1), DT[dt])
+    v, i = B.max_reduction(xc, 1)
+    rv, ri = oracle.max_reduction(x, 1)
+    assert_parity(v, rv, DT[dt])
+    assert torch.equal(i.cpu(), ri)
+    assert torch.equal(B.argmax(xc, 1).cpu(), oracle.argmax(x, 1))
+
+
+@pytest.mark.parametrize("shape,dim,keepdim", [((64, 128), 0, False), ((8, 16, 32), 1, True), ((2, 3, 4, 5), [1, 2], False),
+                                               ((3, 4, 5, 6), [0, 2], True), ((7, 9), -1, False), ((300, 5), 0, True)])
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_reductions_dims(shape, dim, keepdim, dt):
+    x = randn(shape, DT[dt], gen(len(shape) + 40))
+    xc = x.cuda()
+    out = B.mean_reduction(xc, dim, keepdim=keepdim)
+    ref = oracle.mean_reduction(x, dim, keepdim=keepdim)
+    assert out.shape == ref.shape
+    assert_parity(out, ref, DT[dt])
+    if isinstance(dim, int):
+        v, i = B.max_reduction(xc, dim, keepdim)
+        rv, ri = oracle.max_reduction(x, dim, keepdim)
+        assert v.shape == rv.shape and torch.equal(i.cpu(), ri)
+        assert_parity(v, rv, DT[dt])
+        assert torch.equal(B.argmax(xc, dim, keepdim).cpu(), oracle.argmax(x, dim, keepdim))
+
+
+@pytest.mark.parametrize("din,dout", [("bf16", "f32"), ("f32", "bf16"), ("f16", "f32"), ("f32", "f16")])
+def test_mean_dtype_kwarg(din, dout):
+    x = randn((16, 5000), DT[din], gen(77))
+    out = B.mean_reduction(x.cuda(), 1, dtype=DT[dout])
+    assert out.dtype == DT[dout]
+    assert_parity(out, oracle.mean_reduction(x, 1, dtype=DT[dout]), DT[dout])
+
+
+def test_argmax_flatten():
+    x = randn((37, 91), torch.float16, gen(5))
+    assert torch.equal(B.argmax(x.cuda(), None).cpu(), oracle.argmax(x, None))
