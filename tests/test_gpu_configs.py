@@ -29,6 +29,11 @@ def test_full_size_config_matches_oracle(name):
         nv = wl.valid_entries
         for i, (o, r) in enumerate(zip(out, ref)):
             assert_parity(o.reshape(-1)[:nv], r.reshape(-1)[:nv], torch.float32)
+    elif isinstance(ref, tuple):  # max_reduction: (values, indices)
+        assert_parity(out[0], ref[0], ref[0].dtype)
+        assert torch.equal(out[1].cpu(), ref[1])
+    elif not ref.dtype.is_floating_point:  # argmax
+        assert torch.equal(out.cpu(), ref)
     else:
         assert_parity(out, ref, wl.out_dtype, normalised=wl.op in parity.NORMALISED)
 
