@@ -71,7 +71,17 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
     const Tin* xr = static_cast<const Tin*>(a.x) + (rv ? row : 0) * a.N;
     f32x2 sum2 = pk2(0.f, 0.f);
     ArgBest best{kNegInf, INT64_MAX};
+    int64_t best_j0 = -1;  // vector path: first index of the chunk holding best.v
     const int64_t units = rv ? ((V > 1) ? a.nvec : a.N) : 0;
+    Vec16 nx[V > 1 ? U : 1];
+    if constexpr (V > 1) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = t + static_cast<int64_t>(u) * a.tpr;
+        nx[u] = Vec16{{0u, 0u, 0u, 0u}};
+        if (j < units) nx[u] = ld_stream(xr + j * V);
+      }
+    }
     for (int64_t j0 = t; j0 < units; j0 += static_cast<int64_t>(U) * a.tpr) {
       if constexpr (V > 1) {
         constexpr int P = V / 2;
@@ -79,10 +89,16 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
         bool ok[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int64_t j = j0 + static_cast<int64_t>(u) * a.tpr;
-          ok[u] = j < units;
-          v[u] = Vec16{{0u, 0u, 0u, 0u}};
-          if (ok[u]) v[u] = ld_stream(xr + j * V);
+          ok[u] = j0 + static_cast<int64_t>(u) * a.tpr < units;
+          v[u] = nx[u];
+        }
+        // prefetch the next chunk before working on this one
+        const int64_t jn = j0 + static_cast<int64_t>(U) * a.tpr;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t j = jn + static_cast<int64_t>(u) * a.tpr;
+          nx[u] = Vec16{{0u, 0u, 0u, 0u}};
+          if (j < units) nx[u] = ld_stream(xr + j * V);
         }
         if constexpr (OP == kMean) {
 #pragma unroll
@@ -105,24 +121,12 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
               if (!ok[u]) v[u] = Vec16{{ni, ni, ni, ni}};
           }
           const float cm = RawExtreme<Tin, U, false>::run(v);
-          // strictly above the running maximum (a NaN only when none seen yet)
+          // strictly above the running maximum (a NaN only when none seen
+          // yet): remember the chunk; its index is located after the stream
           const bool cn = cm != cm, bn = best.v != best.v;
           if (cn ? !bn : (!bn && cm > best.v)) {
-            // the chunk holds a new maximum: find its first position
-            bool found = false;
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-              float f[V];
-              unpack<Tin>(v[u], f);
-#pragma unroll
-              for (int i = 0; i < V; ++i) {
-                const bool hit = (cm != cm) ? (f[i] != f[i]) : (f[i] == cm);
-                if (!found && hit && ok[u]) {
-                  found = true;
-                  best = ArgBest{cm, (j0 + static_cast<int64_t>(u) * a.tpr) * V + i};
-                }
-              }
-            }
+            best.v = cm;
+            best_j0 = j0;
           }
         }
       } else {
@@ -136,6 +140,29 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
             sum2 = add2(sum2, pk2(f, 0.f));
           } else {
             if (arg_better(f, j, best.v, best.i)) best = ArgBest{f, j};
+          }
+        }
+      }
+    }
+
+    if constexpr (OP != kMean && V > 1) {
+      if (best_j0 >= 0) {
+        // re-read the winning chunk (an L2 hit) and find the first position
+        // of its maximum (or of its first NaN)
+        bool found = false;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t j = best_j0 + static_cast<int64_t>(u) * a.tpr;
+          if (j >= units) continue;
+          float f[V];
+          unpack<Tin>(ld_keep(xr + j * V), f);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const bool hit = (best.v != best.v) ? (f[i] != f[i]) : (f[i] == best.v);
+            if (!found && hit) {
+              found = true;
+              best.i = j * V + i;
+            }
           }
         }
       }
