@@ -228,7 +228,10 @@ inline int round_up32(int v) { return (v + 31) & ~31; }
 template <int OP, typename Tin, typename Tout, int V>
 cudaError_t launch_rows(RedArgs a, cudaStream_t st) {
   const int64_t units = (V > 1) ? a.nvec : a.N;
-  const int64_t per_thread = (V > 1) ? 16 : 64;
+  // Vectors per thread per row: max / argmax pay a fixed per-row cost (the
+  // 64-bit index merge and the re-read of the winning chunk), so they take
+  // longer slices.
+  const int64_t per_thread = (V > 1) ? (OP == kMean ? 16 : 64) : 64;
   int64_t want = (units + per_thread - 1) / per_thread;
   int tpr = static_cast<int>(want > 256 ? 256 : want);
   tpr = round_up32(tpr < 32 ? 32 : tpr);
