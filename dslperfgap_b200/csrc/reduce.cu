@@ -5,9 +5,9 @@
 // [M, N, K] with N the reduced extent:
 //  * reduce_rows_kernel (K == 1): a group of threads per row streams it with
 //    16-byte loads, U vectors in flight per thread. mean accumulates fp32
-//    pairs; max / argmax find each chunk's maximum on the stored values (two
-//    16-bit values per instruction) and only look for its index when the
-//    chunk beats the running maximum.
+//    pairs; max / argmax take each vector's maximum on the stored values (two
+//    16-bit values per instruction), keep the first vector that raises the
+//    running maximum in registers, and locate the element once per row.
 //  * reduce_cols_kernel (K > 1): one thread per (m, k), reads coalesced across k.
 // Index semantics are torch's: the first NaN wins (a NaN is the maximum), and
 // among equal maxima the smallest index wins.
@@ -55,8 +55,8 @@ DSLPG_DEV ArgBest warp_arg_reduce(ArgBest a) {
   return a;
 }
 
-template <int OP, typename Tin, typename Tout, int V>
-__global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
+template <int OP, typename Tin, typename Tout, int V, int MINB = 1>
+__global__ void __launch_bounds__(256, MINB) reduce_rows_kernel(const RedArgs a) {
   constexpr int U = (V == 1) ? 8 : 4;
   __shared__ float red_v[32];
   __shared__ int64_t red_i[32];
@@ -71,7 +71,8 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
     const Tin* xr = static_cast<const Tin*>(a.x) + (rv ? row : 0) * a.N;
     f32x2 sum2 = pk2(0.f, 0.f);
     ArgBest best{kNegInf, INT64_MAX};
-    int64_t best_j0 = -1;  // vector path: first index of the chunk holding best.v
+    int64_t best_j = -1;  // vector path: the vector holding best.v, and its data
+    Vec16 best_vec{{0u, 0u, 0u, 0u}};
     const int64_t units = rv ? ((V > 1) ? a.nvec : a.N) : 0;
     Vec16 nx[V > 1 ? U : 1];
     if constexpr (V > 1) {
@@ -114,19 +115,19 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
               sum2 = add2(sum2, x);  // masked vectors are zeros
             }
         } else {
-          if (!ok[U - 1]) {
-            constexpr uint32_t ni = NegInfWord<Tin>::v;
+          // per vector: its maximum on the stored values; keep the first
+          // vector holding a new running maximum (and its raw data)
 #pragma unroll
-            for (int u = 0; u < U; ++u)
-              if (!ok[u]) v[u] = Vec16{{ni, ni, ni, ni}};
-          }
-          const float cm = RawExtreme<Tin, U, false>::run(v);
-          // strictly above the running maximum (a NaN only when none seen
-          // yet): remember the chunk; its index is located after the stream
-          const bool cn = cm != cm, bn = best.v != best.v;
-          if (cn ? !bn : (!bn && cm > best.v)) {
-            best.v = cm;
-            best_j0 = j0;
+          for (int u = 0; u < U; ++u) {
+            if (!ok[u]) continue;
+            const Vec16 one[1] = {v[u]};
+            const float m = RawExtreme<Tin, 1, false>::run(one);
+            const bool mn = m != m, bn = best.v != best.v;
+            if (mn ? !bn : (!bn && m > best.v)) {
+              best.v = m;
+              best_j = j0 + static_cast<int64_t>(u) * a.tpr;
+              best_vec = v[u];
+            }
           }
         }
       } else {
@@ -146,23 +147,16 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const RedArgs a) {
     }
 
     if constexpr (OP != kMean && V > 1) {
-      if (best_j0 >= 0) {
-        // re-read the winning chunk (an L2 hit) and find the first position
-        // of its maximum (or of its first NaN)
+      if (best_j >= 0) {  // first position of the maximum (or first NaN) in its vector
+        float f[V];
+        unpack<Tin>(best_vec, f);
         bool found = false;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t j = best_j0 + static_cast<int64_t>(u) * a.tpr;
-          if (j >= units) continue;
-          float f[V];
-          unpack<Tin>(ld_keep(xr + j * V), f);
-#pragma unroll
-          for (int i = 0; i < V; ++i) {
-            const bool hit = (best.v != best.v) ? (f[i] != f[i]) : (f[i] == best.v);
-            if (!found && hit) {
-              found = true;
-              best.i = j * V + i;
-            }
+        for (int i = 0; i < V; ++i) {
+          const bool hit = (best.v != best.v) ? (f[i] != f[i]) : (f[i] == best.v);
+          if (!found && hit) {
+            found = true;
+            best.i = best_j * V + i;
           }
         }
       }
@@ -225,7 +219,7 @@ namespace {
 
 inline int round_up32(int v) { return (v + 31) & ~31; }
 
-template <int OP, typename Tin, typename Tout, int V>
+template <int OP, typename Tin, typename Tout, int V, int MINB = 1>
 cudaError_t launch_rows(RedArgs a, cudaStream_t st) {
   const int64_t units = (V > 1) ? a.nvec : a.N;
   // Vectors per thread per row: max / argmax pay a fixed per-row cost (the
@@ -238,9 +232,9 @@ cudaError_t launch_rows(RedArgs a, cudaStream_t st) {
   a.tpr = tpr;
   a.rpc = tpr >= 256 ? 1 : 256 / tpr;
   const int block = a.tpr * a.rpc;
-  const void* fn = reinterpret_cast<const void*>(&reduce_rows_kernel<OP, Tin, Tout, V>);
+  const void* fn = reinterpret_cast<const void*>(&reduce_rows_kernel<OP, Tin, Tout, V, MINB>);
   const int grid = persistent_grid(fn, block, 0, (a.M + a.rpc - 1) / a.rpc);
-  reduce_rows_kernel<OP, Tin, Tout, V><<<grid, block, 0, st>>>(a);
+  reduce_rows_kernel<OP, Tin, Tout, V, MINB><<<grid, block, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -255,6 +249,8 @@ cudaError_t launch_red(RedArgs a, cudaStream_t st) {
   }
   if (aligned(a.x, 16) && a.N % E == 0 && a.N / E <= 0x7fffffff) {
     a.nvec = static_cast<int>(a.N / E);
+    // max / argmax: registers bounded to four CTAs per SM (measured faster)
+    if constexpr (OP != kMean) return launch_rows<OP, Tin, Tout, E, 4>(a, st);
     return launch_rows<OP, Tin, Tout, E>(a, st);
   }
   return launch_rows<OP, Tin, Tout, 1>(a, st);
