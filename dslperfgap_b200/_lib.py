@@ -12,7 +12,11 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libdslpg_b200.so"
+import os
+
+# DSLPG_LIB may name another build of the same library (e.g. one compiled
+# with different cache hints, for a measurement).
+LIB_PATH = Path(os.environ.get("DSLPG_LIB") or Path(__file__).resolve().parent / "lib" / "libdslpg_b200.so")
 
 F32, F16, BF16, I32, I64 = 0, 1, 2, 3, 4
 FLOAT_CODES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}

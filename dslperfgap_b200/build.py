@@ -64,17 +64,21 @@ def _compile(src: Path, obj: Path, extra: list[str], verbose: bool) -> None:
         print(res.stdout + res.stderr, flush=True)
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    """Compile every csrc/*.cu for sm_100a and link lib/libdslpg_b200.so."""
-    BUILD_DIR.mkdir(parents=True, exist_ok=True)
-    LIB_DIR.mkdir(parents=True, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False, defines=(), out: Path | None = None,
+          build_dir: Path | None = None) -> Path:
+    """Compile every csrc/*.cu for sm_100a and link lib/libdslpg_b200.so (or
+    `out`, with extra -D `defines` and objects in `build_dir`)."""
+    lib_path = Path(out) if out else LIB_PATH
+    bdir = Path(build_dir) if build_dir else BUILD_DIR
+    bdir.mkdir(parents=True, exist_ok=True)
+    lib_path.parent.mkdir(parents=True, exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
     hdr_mt = _newest_header_mtime()
-    extra = ["-Xptxas", "-v"] if ptxas_info else []
+    extra = (["-Xptxas", "-v"] if ptxas_info else []) + [f"-D{d}" for d in defines]
     todo = []
     objs = []
     for src in sources:
-        obj = BUILD_DIR / (src.stem + ".o")
+        obj = bdir / (src.stem + ".o")
         objs.append(obj)
         stale = force or ptxas_info or not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, hdr_mt)
         if stale:
@@ -84,15 +88,15 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
             futs = [ex.submit(_compile, s, o, extra, verbose or ptxas_info) for s, o in todo]
             for f in futs:
                 f.result()
-    relink = bool(todo) or not LIB_PATH.exists() or any(o.stat().st_mtime > LIB_PATH.stat().st_mtime for o in objs)
+    relink = bool(todo) or not lib_path.exists() or any(o.stat().st_mtime > lib_path.stat().st_mtime for o in objs)
     if relink:
-        tmp = LIB_DIR / (LIB_NAME + ".tmp")
+        tmp = lib_path.parent / (lib_path.name + ".tmp")
         cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
-        os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+        os.replace(tmp, lib_path)
+    return lib_path
 
 
 def main(argv=None) -> int:
