@@ -49,7 +49,7 @@ SIGNATURES = {
     "dslpg_set_kernel_path": [_c_int],
 }
 
-PATHS = {"auto": 0, "resident": 1, "tma": 2, "stream": 3}
+PATHS = {"auto": 0, "resident": 1, "tma": 2, "stream": 3, "cluster": 4}
 
 _lock = threading.Lock()
 _lib = None

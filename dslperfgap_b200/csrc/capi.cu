@@ -97,7 +97,7 @@ int kernel_path() { return g_path.load(std::memory_order_relaxed); }
 }  // namespace dslpg
 
 extern "C" int dslpg_set_kernel_path(int path) {
-  if (path < DSLPG_PATH_AUTO || path > DSLPG_PATH_STREAM) return DSLPG_ERR_BAD_ARGUMENT;
+  if (path < DSLPG_PATH_AUTO || path > DSLPG_PATH_CLUSTER) return DSLPG_ERR_BAD_ARGUMENT;
   dslpg::g_path.store(path);
   return DSLPG_OK;
 }

@@ -22,6 +22,8 @@
 // (torch semantics: a NaN anywhere in a softmax row poisons the row).
 #include <type_traits>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "pipe.cuh"
 
@@ -603,6 +605,149 @@ __global__ void __launch_bounds__(1024) stream_kernel(const RowArgs a) {
 }
 
 // ============================================================================
+// Cluster kernel: a long row split over the CTAs of a thread-block cluster
+// ============================================================================
+// Partial statistics of a CTA's slice, exchanged through distributed shared
+// memory: (n, mean, m2) for layer_norm, (max, sum of exp) for the softmax
+// family, (sum of squares) for rms_norm.
+struct Part {
+  float a, b, c;
+};
+
+// Each row is split into C contiguous slices of slice_vecs 16-byte vectors,
+// one per CTA of a cluster of C. A CTA copies its slice into shared memory
+// while building its partial statistics, the C partials are exchanged through
+// DSMEM after one cluster barrier (every thread merges them in rank order, so
+// all CTAs hold identical row statistics), and each CTA writes its slice from
+// shared memory: HBM is read once. Clusters loop over rows; the partials are
+// double-buffered, so one cluster barrier per row suffices.
+template <int OP, typename Tin, typename Tout>
+__global__ void __launch_bounds__(512) cluster_norm_kernel(const RowArgs a, int slice_vecs) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ Part part[2];
+  __shared__ float sh_w[96];
+  __shared__ float sh_r[2][32];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  constexpr int E = Elt<Tin>::kPerVec;
+  const int C = static_cast<int>(cl.num_blocks());
+  const int rank = static_cast<int>(cl.block_rank());
+  const int64_t nclusters = gridDim.x / C;
+  const int64_t cid = blockIdx.x / C;
+  const int t = threadIdx.x, T = blockDim.x;
+  const int v0 = rank * slice_vecs;
+  const int nv = max(0, min(a.nvec, v0 + slice_vecs) - v0);
+  Vec16* slice = reinterpret_cast<Vec16*>(smem);
+  int it = 0;
+
+  for (int64_t row = cid; row < a.M; row += nclusters, ++it) {
+    const Tin* xr = static_cast<const Tin*>(a.x) + row * a.N + static_cast<int64_t>(v0) * E;
+    Tout* yr = static_cast<Tout*>(a.y) + row * a.N + static_cast<int64_t>(v0) * E;
+
+    // pass 1: slice -> shared memory, per-thread statistics
+    float ss = 0.f;
+    Welford wf{0.f, 0.f, 0.f};
+    float m = kNegInf, s = 0.f;
+    for (int j = t; j < nv; j += T) {
+      const Vec16 v = ld_stream(xr + static_cast<int64_t>(j) * E);
+      slice[j] = v;
+      float f[E];
+      unpack<Tin>(v, f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
+      if constexpr (OP == kRmsNorm) {
+#pragma unroll
+        for (int i = 0; i < E; ++i) ss = fmaf(f[i], f[i], ss);
+      } else if constexpr (OP == kLayerNorm) {
+        float cs = 0.f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) cs += f[i];
+        const float cmean = cs * (1.0f / E);
+        float cm2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          const float d = f[i] - cmean;
+          cm2 = fmaf(d, d, cm2);
+        }
+        wf = welford_merge(wf, Welford{static_cast<float>(E), cmean, cm2});
+      } else {
+        online_update(m, s, f, E);
+      }
+    }
+
+    // partial of this CTA
+    Part p{0.f, 0.f, 0.f};
+    if constexpr (OP == kRmsNorm) {
+      p.a = group_reduce<SumOp>(ss, sh_r[0], T >> 5, 0);
+    } else if constexpr (OP == kLayerNorm) {
+      wf = block_merge_welford(wf, sh_w);
+      p = Part{wf.n, wf.mean, wf.m2};
+    } else {
+      block_merge_ms(m, s, sh_r[0], sh_r[1]);
+      p = Part{m, s, 0.f};
+    }
+    if (t == 0) part[it & 1] = p;
+    cl.sync();  // partials visible cluster-wide; the slice is complete in shared memory
+
+    // row statistics from the C partials (same order in every thread)
+    float p0 = 0.f, p1 = 0.f;
+    if constexpr (OP == kRmsNorm) {
+      float tot = 0.f;
+      for (int r = 0; r < C; ++r) tot += cl.map_shared_rank(&part[it & 1], r)->a;
+      p0 = rsqrtf(tot * a.inv_n + a.eps);
+    } else if constexpr (OP == kLayerNorm) {
+      Welford tot{0.f, 0.f, 0.f};
+      for (int r = 0; r < C; ++r) {
+        const Part q = *cl.map_shared_rank(&part[it & 1], r);
+        tot = welford_merge(tot, Welford{q.a, q.b, q.c});
+      }
+      p0 = tot.mean;
+      p1 = rsqrtf(tot.m2 * a.inv_n + a.eps);
+    } else {
+      float gm = kNegInf;
+      for (int r = 0; r < C; ++r) gm = max_nan(gm, cl.map_shared_rank(&part[it & 1], r)->a);
+      float gs = 0.f;
+      for (int r = 0; r < C; ++r) {
+        const Part q = *cl.map_shared_rank(&part[it & 1], r);
+        gs += (q.a == gm) ? q.b : q.b * exp_shifted(q.a - gm);
+      }
+      if (!(fabsf(gm) < kPosInf)) gs = __int_as_float(0x7fc00000);  // non-finite max: NaN row
+      p0 = gm;
+      p1 = (OP == kSoftmax) ? 1.0f / gs : logf(gs);
+    }
+
+    // pass 2: the slice from shared memory to the output
+    for (int j = t; j < nv; j += T) {
+      float f[E];
+      unpack<Tin>(slice[j], f);
+#pragma unroll
+      for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
+      if constexpr (OP == kRmsNorm) {
+        float w[E];
+        unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = (f[i] * p0) * w[i];
+      } else if constexpr (OP == kLayerNorm) {
+        float w[E], bb[E];
+        unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
+        unpack<Tin>(weight_vec<Tin>(a.b, v0 + j), bb);
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - p0) * p1, w[i], bb[i]);
+      } else if constexpr (OP == kSoftmax) {
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - p0) * p1;
+      } else {
+#pragma unroll
+        for (int i = 0; i < E; ++i) f[i] = (f[i] - p0) - p1;
+      }
+      StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
+    }
+    __syncthreads();  // the slice buffer is refilled by the next row
+  }
+  cl.sync();  // no CTA leaves while another may still read its partials
+}
+
+// ============================================================================
 // log_softmax over the middle axis of [M, N, K]
 // ============================================================================
 template <typename Tin, typename Tout>
@@ -686,6 +831,46 @@ cudaError_t launch_tma(RowArgs a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Cluster split: slices of at most kClusterSlice bytes, clusters of 2-8 CTAs
+// (portable sizes), rows up to 8 * kClusterSliceMax bytes.
+constexpr uint32_t kClusterSlice = 96u * 1024u;
+constexpr uint32_t kClusterSliceMax = 200u * 1024u;
+
+// Launch the cluster kernel; returns cudaErrorNotSupported when the row does
+// not fit (the caller then streams it).
+template <int OP, typename Tin, typename Tout>
+cudaError_t launch_cluster(RowArgs a, cudaStream_t st) {
+  const int64_t row_bytes = static_cast<int64_t>(a.nvec) * 16;
+  int C = static_cast<int>((row_bytes + kClusterSlice - 1) / kClusterSlice);
+  C = C < 2 ? 2 : (C > 8 ? 8 : C);
+  const int slice_vecs = (a.nvec + C - 1) / C;
+  const size_t smem = static_cast<size_t>(slice_vecs) * 16;
+  if (smem > kClusterSliceMax) return cudaErrorNotSupported;
+  const void* fn = reinterpret_cast<const void*>(&cluster_norm_kernel<OP, Tin, Tout>);
+  if (cudaError_t e = allow_dynamic_smem(fn, smem)) return e;
+  const int block = 512;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int max_clusters = 0;
+  cfg.gridDim = dim3(C * 148);
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, cluster_norm_kernel<OP, Tin, Tout>, &cfg) != cudaSuccess ||
+      max_clusters < 1)
+    max_clusters = sm_count() / C;
+  if (max_clusters < 1) max_clusters = 1;
+  const int64_t nclusters = a.M < max_clusters ? a.M : max_clusters;
+  cfg.gridDim = dim3(static_cast<unsigned>(nclusters * C));
+  return cudaLaunchKernelEx(&cfg, cluster_norm_kernel<OP, Tin, Tout>, a, slice_vecs);
+}
+
 template <int OP, typename Tin, typename Tout>
 cudaError_t dispatch_rows(RowArgs a, cudaStream_t st) {
   constexpr int E = Elt<Tin>::kPerVec;
@@ -710,7 +895,12 @@ cudaError_t dispatch_rows(RowArgs a, cudaStream_t st) {
     // per thread; 8 packed 16-bit vectors per thread do not fit the
     // 64-register budget).
     const int max_resident = (E == 4) ? 8192 : 4096;
-    if (a.nvec <= max_resident && path != DSLPG_PATH_TMA) {
+    if (path == DSLPG_PATH_CLUSTER) {
+      const cudaError_t e = launch_cluster<OP, Tin, Tout>(a, st);
+      if (e != cudaErrorNotSupported) return e;
+      cudaGetLastError();
+    }
+    if (a.nvec <= max_resident && path != DSLPG_PATH_TMA && path != DSLPG_PATH_CLUSTER) {
       // About 16 elements per thread (4 fp32 or 2 16-bit vectors), more only
       // when the row would need more than 1024 threads, fewer for short rows.
       constexpr int kBase = (E == 4) ? 4 : 2;
@@ -730,6 +920,13 @@ cudaError_t dispatch_rows(RowArgs a, cudaStream_t st) {
       }
       if (a.nvec > 32) return launch_resident<OP, Tin, Tout, 2>(a, st);
       return launch_resident<OP, Tin, Tout, 1>(a, st);
+    }
+    // Longer rows: split over a thread-block cluster, the slices resident in
+    // shared memory; rows beyond the cluster's capacity are streamed.
+    if (path != DSLPG_PATH_TMA) {
+      const cudaError_t e = launch_cluster<OP, Tin, Tout>(a, st);
+      if (e != cudaErrorNotSupported) return e;
+      cudaGetLastError();  // clear a not-supported status
     }
     if (vec) return launch_stream<OP, Tin, Tout, E>(a, st);
   }

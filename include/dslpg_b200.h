@@ -62,7 +62,8 @@ enum {
   DSLPG_PATH_AUTO = 0,     /* pick per shape */
   DSLPG_PATH_RESIDENT = 1, /* rows read straight into registers */
   DSLPG_PATH_TMA = 2,      /* rows / row chunks staged by TMA bulk copies */
-  DSLPG_PATH_STREAM = 3    /* two-pass streaming (any length or alignment) */
+  DSLPG_PATH_STREAM = 3,   /* two-pass streaming (any length or alignment) */
+  DSLPG_PATH_CLUSTER = 4   /* a row split over a thread-block cluster (DSMEM exchange) */
 };
 
 /* Select the kernel shape for subsequent calls (process-wide). A path that

@@ -43,7 +43,7 @@ def test_python_binding_covers_header():
 def test_kernel_path_validation(lib):
     assert lib.dslpg_set_kernel_path(9) == -5
     assert lib.dslpg_set_kernel_path(-1) == -5
-    for code in range(4):
+    for code in range(5):
         assert lib.dslpg_set_kernel_path(code) == 0
     assert lib.dslpg_set_kernel_path(0) == 0
 

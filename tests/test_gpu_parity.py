@@ -20,7 +20,7 @@ from dslperfgap_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
-PATHS = ["auto", "resident", "tma", "stream"]
+PATHS = ["auto", "resident", "tma", "stream", "cluster"]
 
 
 @pytest.fixture(params=PATHS)
@@ -31,7 +31,7 @@ def path(request):
 
 
 LENGTHS = [1, 7, 32, 64, 100, 128, 256, 512, 1000, 1024, 2048, 4096, 5120, 8192, 12288, 16384, 32768,
-           40000, 65536, 131072]
+           40000, 65536, 131072, 262144, 1048576]
 
 
 def gen(seed):
