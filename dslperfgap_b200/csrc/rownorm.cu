@@ -615,18 +615,27 @@ struct Part {
 };
 
 // Each row is split into C contiguous slices of slice_vecs 16-byte vectors,
-// one per CTA of a cluster of C. A CTA copies its slice into shared memory
-// while building its partial statistics, the C partials are exchanged through
-// DSMEM after one cluster barrier (every thread merges them in rank order, so
-// all CTAs hold identical row statistics), and each CTA writes its slice from
-// shared memory: HBM is read once. Clusters loop over rows; the partials are
-// double-buffered, so one cluster barrier per row suffices.
+// one per CTA of a cluster of C. A CTA's slice is staged into shared memory by
+// TMA bulk copies (cp.async.bulk into the CTA's own shared memory, no
+// multicast), double-buffered: the next row's slice is in flight while this
+// row is reduced. The CTA builds its partial statistics from shared memory;
+// the C partials are exchanged through DSMEM after one cluster barrier (every
+// thread merges them in rank order, so all CTAs hold identical row
+// statistics); each CTA then writes its slice from shared memory, so HBM is
+// read once. Clusters loop over rows; partials are double-buffered, so one
+// cluster barrier per row suffices. Waits on the copies are bounded as in the
+// other pipelines; after a timeout the loop keeps its shape (the cluster
+// barriers stay matched) but skips waits and stores.
+static __device__ unsigned int g_cluster_timeouts;
+
 template <int OP, typename Tin, typename Tout>
 __global__ void __launch_bounds__(512) cluster_norm_kernel(const RowArgs a, int slice_vecs) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ Part part[2];
   __shared__ float sh_w[96];
   __shared__ float sh_r[2][32];
+  __shared__ __align__(8) unsigned long long bars[2];
+  __shared__ volatile int abort_flag;
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   constexpr int E = Elt<Tin>::kPerVec;
@@ -637,22 +646,59 @@ __global__ void __launch_bounds__(512) cluster_norm_kernel(const RowArgs a, int 
   const int t = threadIdx.x, T = blockDim.x;
   const int v0 = rank * slice_vecs;
   const int nv = max(0, min(a.nvec, v0 + slice_vecs) - v0);
-  Vec16* slice = reinterpret_cast<Vec16*>(smem);
-  int it = 0;
+  const uint32_t slice_bytes = static_cast<uint32_t>(nv) * 16u;
+  const uint32_t buf0 = smem_u32(smem);
+  const uint32_t bar0 = smem_u32(&bars[0]);
+  if (t == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar0 + 8, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
 
+  uint64_t pol = 0;
+  if (t == 0) pol = l2_evict_first_policy();
+  auto issue = [&](int64_t row, int b) {  // thread 0: slice of `row` into buffer b
+    if (slice_bytes == 0) {
+      mbar_arrive(bar0 + 8u * b);
+      return;
+    }
+    mbar_arrive_expect_tx(bar0 + 8u * b, slice_bytes);
+    const char* src = reinterpret_cast<const char*>(static_cast<const Tin*>(a.x) + row * a.N) +
+                      static_cast<int64_t>(v0) * 16;
+    const uint32_t dst = buf0 + static_cast<uint32_t>(b) * static_cast<uint32_t>(slice_vecs) * 16u;
+    for (uint32_t off = 0; off < slice_bytes; off += 32768u) {
+      const uint32_t n = (slice_bytes - off) < 32768u ? (slice_bytes - off) : 32768u;
+      bulk_load(dst + off, src + off, n, bar0 + 8u * b, pol);
+    }
+  };
+  if (t == 0 && cid < a.M) issue(cid, 0);
+  int issued = (cid < a.M) ? 1 : 0;  // uses of the buffers so far (thread 0)
+
+  int it = 0;
   for (int64_t row = cid; row < a.M; row += nclusters, ++it) {
-    const Tin* xr = static_cast<const Tin*>(a.x) + row * a.N + static_cast<int64_t>(v0) * E;
+    const int b = it & 1;
+    // prefetch the next row into the other buffer (its last reader, row
+    // it - 1, finished before the barrier that ended that iteration)
+    if (t == 0 && row + nclusters < a.M && !abort_flag) {
+      issue(row + nclusters, b ^ 1);
+      ++issued;
+    }
+    if (!abort_flag && !mbar_wait(bar0 + 8u * b, (it >> 1) & 1, kWaitLimitNs)) {
+      atomicAdd(&g_cluster_timeouts, 1u);
+      abort_flag = 1;
+    }
+    const Vec16* slice = reinterpret_cast<const Vec16*>(smem) + static_cast<int64_t>(b) * slice_vecs;
     Tout* yr = static_cast<Tout*>(a.y) + row * a.N + static_cast<int64_t>(v0) * E;
 
-    // pass 1: slice -> shared memory, per-thread statistics
+    // pass 1: per-thread statistics of the slice
     float ss = 0.f;
     Welford wf{0.f, 0.f, 0.f};
     float m = kNegInf, s = 0.f;
     for (int j = t; j < nv; j += T) {
-      const Vec16 v = ld_stream(xr + static_cast<int64_t>(j) * E);
-      slice[j] = v;
       float f[E];
-      unpack<Tin>(v, f);
+      unpack<Tin>(slice[j], f);
 #pragma unroll
       for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
       if constexpr (OP == kRmsNorm) {
@@ -687,7 +733,7 @@ __global__ void __launch_bounds__(512) cluster_norm_kernel(const RowArgs a, int 
       p = Part{m, s, 0.f};
     }
     if (t == 0) part[it & 1] = p;
-    cl.sync();  // partials visible cluster-wide; the slice is complete in shared memory
+    cl.sync();  // partials visible cluster-wide
 
     // row statistics from the C partials (same order in every thread)
     float p0 = 0.f, p1 = 0.f;
@@ -717,32 +763,39 @@ __global__ void __launch_bounds__(512) cluster_norm_kernel(const RowArgs a, int 
     }
 
     // pass 2: the slice from shared memory to the output
-    for (int j = t; j < nv; j += T) {
-      float f[E];
-      unpack<Tin>(slice[j], f);
+    if (!abort_flag) {
+      for (int j = t; j < nv; j += T) {
+        float f[E];
+        unpack<Tin>(slice[j], f);
 #pragma unroll
-      for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
-      if constexpr (OP == kRmsNorm) {
-        float w[E];
-        unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
+        for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
+        if constexpr (OP == kRmsNorm) {
+          float w[E];
+          unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
 #pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = (f[i] * p0) * w[i];
-      } else if constexpr (OP == kLayerNorm) {
-        float w[E], bb[E];
-        unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
-        unpack<Tin>(weight_vec<Tin>(a.b, v0 + j), bb);
+          for (int i = 0; i < E; ++i) f[i] = (f[i] * p0) * w[i];
+        } else if constexpr (OP == kLayerNorm) {
+          float w[E], bb[E];
+          unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
+          unpack<Tin>(weight_vec<Tin>(a.b, v0 + j), bb);
 #pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - p0) * p1, w[i], bb[i]);
-      } else if constexpr (OP == kSoftmax) {
+          for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - p0) * p1, w[i], bb[i]);
+        } else if constexpr (OP == kSoftmax) {
 #pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - p0) * p1;
-      } else {
+          for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - p0) * p1;
+        } else {
 #pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = (f[i] - p0) - p1;
+          for (int i = 0; i < E; ++i) f[i] = (f[i] - p0) - p1;
+        }
+        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
       }
-      StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
     }
-    __syncthreads();  // the slice buffer is refilled by the next row
+    __syncthreads();  // this buffer is refilled two rows later
+  }
+  // no copy may still be landing in shared memory when the CTA exits
+  if (t == 0) {
+    for (int u = (issued > 2 ? issued - 2 : 0); u < issued; ++u)
+      if (!mbar_wait(bar0 + 8u * (u & 1), (u >> 1) & 1, kWaitLimitNs)) atomicAdd(&g_cluster_timeouts, 1u);
   }
   cl.sync();  // no CTA leaves while another may still read its partials
 }
@@ -831,10 +884,11 @@ cudaError_t launch_tma(RowArgs a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// Cluster split: slices of at most kClusterSlice bytes, clusters of 2-8 CTAs
-// (portable sizes), rows up to 8 * kClusterSliceMax bytes.
-constexpr uint32_t kClusterSlice = 96u * 1024u;
-constexpr uint32_t kClusterSliceMax = 200u * 1024u;
+// Cluster split: slices of about kClusterSlice bytes, clusters of 2-8 CTAs
+// (portable sizes), two slice buffers per CTA, so rows up to
+// 8 * kClusterSliceMax bytes.
+constexpr uint32_t kClusterSlice = 48u * 1024u;
+constexpr uint32_t kClusterSliceMax = 100u * 1024u;
 
 // Launch the cluster kernel; returns cudaErrorNotSupported when the row does
 // not fit (the caller then streams it).
@@ -844,8 +898,8 @@ cudaError_t launch_cluster(RowArgs a, cudaStream_t st) {
   int C = static_cast<int>((row_bytes + kClusterSlice - 1) / kClusterSlice);
   C = C < 2 ? 2 : (C > 8 ? 8 : C);
   const int slice_vecs = (a.nvec + C - 1) / C;
-  const size_t smem = static_cast<size_t>(slice_vecs) * 16;
-  if (smem > kClusterSliceMax) return cudaErrorNotSupported;
+  if (static_cast<size_t>(slice_vecs) * 16 > kClusterSliceMax) return cudaErrorNotSupported;
+  const size_t smem = 2 * static_cast<size_t>(slice_vecs) * 16;
   const void* fn = reinterpret_cast<const void*>(&cluster_norm_kernel<OP, Tin, Tout>);
   if (cudaError_t e = allow_dynamic_smem(fn, smem)) return e;
   const int block = 512;
@@ -1070,9 +1124,11 @@ extern "C" int dslpg_log_softmax_fwd(const void* x, void* y, int64_t M, int64_t 
 
 namespace dslpg {
 unsigned int take_wait_timeouts_rownorm() {
-  unsigned int v = 0, zero = 0;
+  unsigned int v = 0, w = 0, zero = 0;
   cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
   cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero));
-  return v;
+  cudaMemcpyFromSymbol(&w, g_cluster_timeouts, sizeof(w));
+  cudaMemcpyToSymbol(g_cluster_timeouts, &zero, sizeof(zero));
+  return v + w;
 }
 }  // namespace dslpg
