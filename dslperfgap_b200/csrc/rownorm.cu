@@ -607,35 +607,38 @@ __global__ void __launch_bounds__(1024) stream_kernel(const RowArgs a) {
 // ============================================================================
 // Cluster kernel: a long row split over the CTAs of a thread-block cluster
 // ============================================================================
-// Partial statistics of a CTA's slice, exchanged through distributed shared
-// memory: (n, mean, m2) for layer_norm, (max, sum of exp) for the softmax
-// family, (sum of squares) for rms_norm.
-struct Part {
-  float a, b, c;
+// Reductions over a whole cluster: a CTA-wide reduction, the C per-CTA values
+// exchanged through distributed shared memory after one cluster barrier, and
+// combined in rank order by every thread (so all CTAs agree bit for bit). The
+// exchange slots are double-buffered: a slot is rewritten two reductions
+// later, after a cluster barrier that follows every read of it.
+struct ClusterReducer {
+  float* slots;  // [2] in this CTA's shared memory
+  float (*red)[32];
+  int buf, C;
+  template <class Op> DSLPG_DEV float reduce(float v) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    v = group_reduce<Op>(v, red[buf], blockDim.x >> 5, 0);
+    if (threadIdx.x == 0) slots[buf] = v;
+    cl.sync();
+    float r = *cl.map_shared_rank(&slots[buf], 0);
+    for (int q = 1; q < C; ++q) r = Op::apply(r, *cl.map_shared_rank(&slots[buf], q));
+    buf ^= 1;
+    return r;
+  }
 };
 
 // Each row is split into C contiguous slices of slice_vecs 16-byte vectors,
-// one per CTA of a cluster of C. A CTA's slice is staged into shared memory by
-// TMA bulk copies (cp.async.bulk into the CTA's own shared memory, no
-// multicast), double-buffered: the next row's slice is in flight while this
-// row is reduced. The CTA builds its partial statistics from shared memory;
-// the C partials are exchanged through DSMEM after one cluster barrier (every
-// thread merges them in rank order, so all CTAs hold identical row
-// statistics); each CTA then writes its slice from shared memory, so HBM is
-// read once. Clusters loop over rows; partials are double-buffered, so one
-// cluster barrier per row suffices. Waits on the copies are bounded as in the
-// other pipelines; after a timeout the loop keeps its shape (the cluster
-// barriers stay matched) but skips waits and stores.
-static __device__ unsigned int g_cluster_timeouts;
-
-template <int OP, typename Tin, typename Tout>
-__global__ void __launch_bounds__(512) cluster_norm_kernel(const RowArgs a, int slice_vecs) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ Part part[2];
-  __shared__ float sh_w[96];
-  __shared__ float sh_r[2][32];
-  __shared__ __align__(8) unsigned long long bars[2];
-  __shared__ volatile int abort_flag;
+// one per CTA of a cluster of C (up to 8 portable CTAs of 1024 threads). A CTA
+// holds its slice in registers, VPT vectors per thread, prefetching the next
+// row's slice while it reduces this one, exactly as the resident kernel does
+// within one CTA; the row statistics come from ClusterReducer. HBM is read
+// once and written once. Clusters loop over rows.
+template <int OP, typename Tin, typename Tout, int VPT>
+__global__ void __launch_bounds__(1024) cluster_norm_kernel(const RowArgs a, int slice_vecs) {
+  __shared__ float red[2][32];
+  __shared__ float slots[2];
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   constexpr int E = Elt<Tin>::kPerVec;
@@ -643,161 +646,41 @@ __global__ void __launch_bounds__(512) cluster_norm_kernel(const RowArgs a, int 
   const int rank = static_cast<int>(cl.block_rank());
   const int64_t nclusters = gridDim.x / C;
   const int64_t cid = blockIdx.x / C;
-  const int t = threadIdx.x, T = blockDim.x;
+  const int t = threadIdx.x;
   const int v0 = rank * slice_vecs;
   const int nv = max(0, min(a.nvec, v0 + slice_vecs) - v0);
-  const uint32_t slice_bytes = static_cast<uint32_t>(nv) * 16u;
-  const uint32_t buf0 = smem_u32(smem);
-  const uint32_t bar0 = smem_u32(&bars[0]);
-  if (t == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar0 + 8, 1);
-    fence_mbar_init();
-    abort_flag = 0;
-  }
-  __syncthreads();
 
-  uint64_t pol = 0;
-  if (t == 0) pol = l2_evict_first_policy();
-  auto issue = [&](int64_t row, int b) {  // thread 0: slice of `row` into buffer b
-    if (slice_bytes == 0) {
-      mbar_arrive(bar0 + 8u * b);
-      return;
-    }
-    mbar_arrive_expect_tx(bar0 + 8u * b, slice_bytes);
-    const char* src = reinterpret_cast<const char*>(static_cast<const Tin*>(a.x) + row * a.N) +
-                      static_cast<int64_t>(v0) * 16;
-    const uint32_t dst = buf0 + static_cast<uint32_t>(b) * static_cast<uint32_t>(slice_vecs) * 16u;
-    for (uint32_t off = 0; off < slice_bytes; off += 32768u) {
-      const uint32_t n = (slice_bytes - off) < 32768u ? (slice_bytes - off) : 32768u;
-      bulk_load(dst + off, src + off, n, bar0 + 8u * b, pol);
+  // The slice seen as a row of its own (statistics still use 1/N of the row).
+  RowArgs s = a;
+  s.tpr = blockDim.x;
+  s.nvec = nv;
+  if (a.w) s.w = static_cast<const Tin*>(a.w) + static_cast<int64_t>(v0) * E;
+  if (a.b) s.b = static_cast<const Tin*>(a.b) + static_cast<int64_t>(v0) * E;
+  ClusterReducer rd{slots, red, 0, C};
+
+  auto load_row = [&](Vec16* dst, int64_t row) {
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int j = t + k * s.tpr;
+      dst[k] = Vec16{{0u, 0u, 0u, 0u}};
+      if (row < a.M && j < nv)
+        dst[k] = ld_stream(static_cast<const Tin*>(a.x) + row * a.N + static_cast<int64_t>(v0 + j) * E);
     }
   };
-  if (t == 0 && cid < a.M) issue(cid, 0);
-  int issued = (cid < a.M) ? 1 : 0;  // uses of the buffers so far (thread 0)
-
-  int it = 0;
-  for (int64_t row = cid; row < a.M; row += nclusters, ++it) {
-    const int b = it & 1;
-    // prefetch the next row into the other buffer (its last reader, row
-    // it - 1, finished before the barrier that ended that iteration)
-    if (t == 0 && row + nclusters < a.M && !abort_flag) {
-      issue(row + nclusters, b ^ 1);
-      ++issued;
-    }
-    if (!abort_flag && !mbar_wait(bar0 + 8u * b, (it >> 1) & 1, kWaitLimitNs)) {
-      atomicAdd(&g_cluster_timeouts, 1u);
-      abort_flag = 1;
-    }
-    const Vec16* slice = reinterpret_cast<const Vec16*>(smem) + static_cast<int64_t>(b) * slice_vecs;
-    Tout* yr = static_cast<Tout*>(a.y) + row * a.N + static_cast<int64_t>(v0) * E;
-
-    // pass 1: per-thread statistics of the slice
-    float ss = 0.f;
-    Welford wf{0.f, 0.f, 0.f};
-    float m = kNegInf, s = 0.f;
-    for (int j = t; j < nv; j += T) {
-      float f[E];
-      unpack<Tin>(slice[j], f);
+  Vec16 nxt[VPT];
+  load_row(nxt, cid);
+  for (int64_t row = cid; row < a.M; row += nclusters) {
+    Vec16 v[VPT];
 #pragma unroll
-      for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
-      if constexpr (OP == kRmsNorm) {
+    for (int k = 0; k < VPT; ++k) v[k] = nxt[k];
+    load_row(nxt, row + nclusters);
+    bool ok[VPT];
 #pragma unroll
-        for (int i = 0; i < E; ++i) ss = fmaf(f[i], f[i], ss);
-      } else if constexpr (OP == kLayerNorm) {
-        float cs = 0.f;
-#pragma unroll
-        for (int i = 0; i < E; ++i) cs += f[i];
-        const float cmean = cs * (1.0f / E);
-        float cm2 = 0.f;
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const float d = f[i] - cmean;
-          cm2 = fmaf(d, d, cm2);
-        }
-        wf = welford_merge(wf, Welford{static_cast<float>(E), cmean, cm2});
-      } else {
-        online_update(m, s, f, E);
-      }
-    }
-
-    // partial of this CTA
-    Part p{0.f, 0.f, 0.f};
-    if constexpr (OP == kRmsNorm) {
-      p.a = group_reduce<SumOp>(ss, sh_r[0], T >> 5, 0);
-    } else if constexpr (OP == kLayerNorm) {
-      wf = block_merge_welford(wf, sh_w);
-      p = Part{wf.n, wf.mean, wf.m2};
-    } else {
-      block_merge_ms(m, s, sh_r[0], sh_r[1]);
-      p = Part{m, s, 0.f};
-    }
-    if (t == 0) part[it & 1] = p;
-    cl.sync();  // partials visible cluster-wide
-
-    // row statistics from the C partials (same order in every thread)
-    float p0 = 0.f, p1 = 0.f;
-    if constexpr (OP == kRmsNorm) {
-      float tot = 0.f;
-      for (int r = 0; r < C; ++r) tot += cl.map_shared_rank(&part[it & 1], r)->a;
-      p0 = rsqrtf(tot * a.inv_n + a.eps);
-    } else if constexpr (OP == kLayerNorm) {
-      Welford tot{0.f, 0.f, 0.f};
-      for (int r = 0; r < C; ++r) {
-        const Part q = *cl.map_shared_rank(&part[it & 1], r);
-        tot = welford_merge(tot, Welford{q.a, q.b, q.c});
-      }
-      p0 = tot.mean;
-      p1 = rsqrtf(tot.m2 * a.inv_n + a.eps);
-    } else {
-      float gm = kNegInf;
-      for (int r = 0; r < C; ++r) gm = max_nan(gm, cl.map_shared_rank(&part[it & 1], r)->a);
-      float gs = 0.f;
-      for (int r = 0; r < C; ++r) {
-        const Part q = *cl.map_shared_rank(&part[it & 1], r);
-        gs += (q.a == gm) ? q.b : q.b * exp_shifted(q.a - gm);
-      }
-      if (!(fabsf(gm) < kPosInf)) gs = __int_as_float(0x7fc00000);  // non-finite max: NaN row
-      p0 = gm;
-      p1 = (OP == kSoftmax) ? 1.0f / gs : logf(gs);
-    }
-
-    // pass 2: the slice from shared memory to the output
-    if (!abort_flag) {
-      for (int j = t; j < nv; j += T) {
-        float f[E];
-        unpack<Tin>(slice[j], f);
-#pragma unroll
-        for (int i = 0; i < E; ++i) f[i] = in_value<Tin, Tout>(f[i]);
-        if constexpr (OP == kRmsNorm) {
-          float w[E];
-          unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
-#pragma unroll
-          for (int i = 0; i < E; ++i) f[i] = (f[i] * p0) * w[i];
-        } else if constexpr (OP == kLayerNorm) {
-          float w[E], bb[E];
-          unpack<Tin>(weight_vec<Tin>(a.w, v0 + j), w);
-          unpack<Tin>(weight_vec<Tin>(a.b, v0 + j), bb);
-#pragma unroll
-          for (int i = 0; i < E; ++i) f[i] = fmaf((f[i] - p0) * p1, w[i], bb[i]);
-        } else if constexpr (OP == kSoftmax) {
-#pragma unroll
-          for (int i = 0; i < E; ++i) f[i] = exp_shifted(f[i] - p0) * p1;
-        } else {
-#pragma unroll
-          for (int i = 0; i < E; ++i) f[i] = (f[i] - p0) - p1;
-        }
-        StoreOut<Tout, E>::run(yr + static_cast<int64_t>(j) * E, f);
-      }
-    }
-    __syncthreads();  // this buffer is refilled two rows later
+    for (int k = 0; k < VPT; ++k) ok[k] = (t + k * s.tpr) < nv;
+    normalize_row<OP, Tin, Tout, VPT, (OP == kLogSoftmax ? 0 : 16)>(
+        s, v, ok, t, static_cast<Tout*>(a.y) + row * a.N + static_cast<int64_t>(v0) * E, rd);
   }
-  // no copy may still be landing in shared memory when the CTA exits
-  if (t == 0) {
-    for (int u = (issued > 2 ? issued - 2 : 0); u < issued; ++u)
-      if (!mbar_wait(bar0 + 8u * (u & 1), (u >> 1) & 1, kWaitLimitNs)) atomicAdd(&g_cluster_timeouts, 1u);
-  }
-  cl.sync();  // no CTA leaves while another may still read its partials
+  cl.sync();  // no CTA leaves while another may still read its exchange slots
 }
 
 // ============================================================================
@@ -884,25 +767,13 @@ cudaError_t launch_tma(RowArgs a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// Cluster split: slices of about kClusterSlice bytes, clusters of 2-8 CTAs
-// (portable sizes), two slice buffers per CTA, so rows up to
-// 8 * kClusterSliceMax bytes.
-constexpr uint32_t kClusterSlice = 48u * 1024u;
-constexpr uint32_t kClusterSliceMax = 100u * 1024u;
-
-// Launch the cluster kernel; returns cudaErrorNotSupported when the row does
-// not fit (the caller then streams it).
-template <int OP, typename Tin, typename Tout>
-cudaError_t launch_cluster(RowArgs a, cudaStream_t st) {
-  const int64_t row_bytes = static_cast<int64_t>(a.nvec) * 16;
-  int C = static_cast<int>((row_bytes + kClusterSlice - 1) / kClusterSlice);
-  C = C < 2 ? 2 : (C > 8 ? 8 : C);
+// Cluster split: 1024-thread CTAs holding VPT vectors per thread, clusters of
+// 2-8 CTAs (portable sizes): rows up to 8 * 1024 * 4 vectors (512 KiB of
+// 16-bit data, 1 MiB of fp32 with 8 vectors per thread).
+template <int OP, typename Tin, typename Tout, int VPT>
+cudaError_t launch_cluster_v(RowArgs a, int C, cudaStream_t st) {
   const int slice_vecs = (a.nvec + C - 1) / C;
-  if (static_cast<size_t>(slice_vecs) * 16 > kClusterSliceMax) return cudaErrorNotSupported;
-  const size_t smem = 2 * static_cast<size_t>(slice_vecs) * 16;
-  const void* fn = reinterpret_cast<const void*>(&cluster_norm_kernel<OP, Tin, Tout>);
-  if (cudaError_t e = allow_dynamic_smem(fn, smem)) return e;
-  const int block = 512;
+  const int block = 1024;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -910,19 +781,36 @@ cudaError_t launch_cluster(RowArgs a, cudaStream_t st) {
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(block);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  cfg.gridDim = dim3(C * sm_count());
   int max_clusters = 0;
-  cfg.gridDim = dim3(C * 148);
-  if (cudaOccupancyMaxActiveClusters(&max_clusters, cluster_norm_kernel<OP, Tin, Tout>, &cfg) != cudaSuccess ||
-      max_clusters < 1)
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, cluster_norm_kernel<OP, Tin, Tout, VPT>, &cfg) != cudaSuccess ||
+      max_clusters < 1) {
+    cudaGetLastError();
     max_clusters = sm_count() / C;
+  }
   if (max_clusters < 1) max_clusters = 1;
   const int64_t nclusters = a.M < max_clusters ? a.M : max_clusters;
   cfg.gridDim = dim3(static_cast<unsigned>(nclusters * C));
-  return cudaLaunchKernelEx(&cfg, cluster_norm_kernel<OP, Tin, Tout>, a, slice_vecs);
+  return cudaLaunchKernelEx(&cfg, cluster_norm_kernel<OP, Tin, Tout, VPT>, a, slice_vecs);
+}
+
+// Launch the cluster kernel; returns cudaErrorNotSupported when the row does
+// not fit (the caller then streams it).
+template <int OP, typename Tin, typename Tout>
+cudaError_t launch_cluster(RowArgs a, cudaStream_t st) {
+  constexpr int E = Elt<Tin>::kPerVec;
+  constexpr int kVpt = (E == 4) ? 4 : 2;  // 16 elements per thread, as the resident kernel
+  int C = (a.nvec + 1024 * kVpt - 1) / (1024 * kVpt);
+  if (C < 2) C = 2;
+  if (C <= 8) return launch_cluster_v<OP, Tin, Tout, kVpt>(a, C, st);
+  // twice the vectors per thread
+  C = (a.nvec + 1024 * 2 * kVpt - 1) / (1024 * 2 * kVpt);
+  if (C <= 8) return launch_cluster_v<OP, Tin, Tout, 2 * kVpt>(a, C, st);
+  return cudaErrorNotSupported;
 }
 
 template <int OP, typename Tin, typename Tout>
@@ -1124,11 +1012,9 @@ extern "C" int dslpg_log_softmax_fwd(const void* x, void* y, int64_t M, int64_t 
 
 namespace dslpg {
 unsigned int take_wait_timeouts_rownorm() {
-  unsigned int v = 0, w = 0, zero = 0;
+  unsigned int v = 0, zero = 0;
   cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
   cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero));
-  cudaMemcpyFromSymbol(&w, g_cluster_timeouts, sizeof(w));
-  cudaMemcpyToSymbol(g_cluster_timeouts, &zero, sizeof(zero));
-  return v + w;
+  return v;
 }
 }  // namespace dslpg
