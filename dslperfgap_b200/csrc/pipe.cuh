@@ -16,6 +16,8 @@
 // copies it issued before the CTA exits, so no copy is left in flight.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace dslpg {
@@ -133,6 +135,28 @@ struct ConsumerReducer {
     v = consumer_reduce<Op>(v, red + 32 * buf, ncw);
     buf ^= 1;
     return v;
+  }
+};
+
+// Reductions over a whole cluster: a CTA-wide reduction, the C per-CTA values
+// exchanged through distributed shared memory after one cluster barrier, and
+// combined in rank order by every thread (so all CTAs agree bit for bit). The
+// exchange slots are double-buffered: a slot is rewritten two reductions
+// later, after a cluster barrier that follows every read of it.
+struct ClusterReducer {
+  float* slots;  // [2] in this CTA's shared memory
+  float (*red)[32];
+  int buf, C;
+  template <class Op> DSLPG_DEV float reduce(float v) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    v = group_reduce<Op>(v, red[buf], blockDim.x >> 5, 0);
+    if (threadIdx.x == 0) slots[buf] = v;
+    cl.sync();
+    float r = *cl.map_shared_rank(&slots[buf], 0);
+    for (int q = 1; q < C; ++q) r = Op::apply(r, *cl.map_shared_rank(&slots[buf], q));
+    buf ^= 1;
+    return r;
   }
 };
 

@@ -607,28 +607,6 @@ __global__ void __launch_bounds__(1024) stream_kernel(const RowArgs a) {
 // ============================================================================
 // Cluster kernel: a long row split over the CTAs of a thread-block cluster
 // ============================================================================
-// Reductions over a whole cluster: a CTA-wide reduction, the C per-CTA values
-// exchanged through distributed shared memory after one cluster barrier, and
-// combined in rank order by every thread (so all CTAs agree bit for bit). The
-// exchange slots are double-buffered: a slot is rewritten two reductions
-// later, after a cluster barrier that follows every read of it.
-struct ClusterReducer {
-  float* slots;  // [2] in this CTA's shared memory
-  float (*red)[32];
-  int buf, C;
-  template <class Op> DSLPG_DEV float reduce(float v) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cl = cg::this_cluster();
-    v = group_reduce<Op>(v, red[buf], blockDim.x >> 5, 0);
-    if (threadIdx.x == 0) slots[buf] = v;
-    cl.sync();
-    float r = *cl.map_shared_rank(&slots[buf], 0);
-    for (int q = 1; q < C; ++q) r = Op::apply(r, *cl.map_shared_rank(&slots[buf], q));
-    buf ^= 1;
-    return r;
-  }
-};
-
 // Each row is split into C contiguous slices of slice_vecs 16-byte vectors,
 // one per CTA of a cluster of C (up to 8 portable CTAs of 1024 threads). A CTA
 // holds its slice in registers, VPT vectors per thread, prefetching the next

@@ -342,6 +342,67 @@ __global__ void __launch_bounds__(544) tma_stat_kernel(const StatArgs a, int sta
   }
 }
 
+// Few long work items: each item split over the CTAs of a thread-block
+// cluster. Every CTA folds its contiguous slice of the item (the same online
+// fold as rowstat_kernel, next loads prefetched), the per-CTA (max, sum[, x
+// sum]) are merged through distributed shared memory (ClusterReducer), and
+// rank 0 writes the item's results. Clusters loop over items.
+template <int KIND, typename T, bool SMOOTH>
+__global__ void __launch_bounds__(512) cluster_stat_kernel(const StatArgs a, int64_t slice_vecs) {
+  constexpr int V = Elt<T>::kPerVec;
+  constexpr int U = 4;
+  __shared__ float red[2][32];
+  __shared__ float slots[2];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = static_cast<int>(cl.num_blocks());
+  const int rank = static_cast<int>(cl.block_rank());
+  const int64_t nclusters = gridDim.x / C;
+  const int64_t cid = blockIdx.x / C;
+  const int t = threadIdx.x, nt = blockDim.x;
+  const int64_t items = a.M * a.nseg;
+  ClusterReducer rd{slots, red, 0, C};
+
+  for (int64_t item = cid; item < items; item += nclusters) {
+    const int64_t r = item / a.nseg, cb = item - r * a.nseg;
+    const int64_t col0 = cb * a.seg;
+    const int64_t len = (a.N - col0) < a.seg ? (a.N - col0) : a.seg;
+    const int64_t nvi = len / V;
+    const int64_t j_lo = rank * slice_vecs;
+    const int64_t j_hi = (j_lo + slice_vecs) < nvi ? (j_lo + slice_vecs) : nvi;
+    const T* xs = static_cast<const T*>(a.x) + r * a.ld + col0;
+    float m = kNegInf, s = 0.f, sum = 0.f;
+    auto load = [&](Vec16 (&dst)[U], int64_t j0) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = j0 + static_cast<int64_t>(u) * nt;
+        dst[u] = Vec16{{0u, 0u, 0u, 0u}};
+        if (j < j_hi) dst[u] = ld_stream(xs + j * V);
+      }
+    };
+    Vec16 nx[U];
+    load(nx, j_lo + t);
+    for (int64_t j0 = j_lo + t; j0 < j_hi; j0 += static_cast<int64_t>(U) * nt) {
+      Vec16 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = nx[u];
+      load(nx, j0 + static_cast<int64_t>(U) * nt);
+      bool ok[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) ok[u] = j0 + static_cast<int64_t>(u) * nt < j_hi;
+      if (ok[U - 1]) fold_vecs<T, U, SMOOTH, 4>(m, s, sum, v, a.c);
+      else fold_vecs_masked<T, U, SMOOTH>(m, s, sum, v, ok, a.c);
+    }
+    const float gm = rd.template reduce<MaxOp>(m);
+    const float sc = (m == gm) ? s : s * ex2(m - gm);
+    const float gs = rd.template reduce<SumOp>(sc);
+    float gsum = 0.f;
+    if constexpr (SMOOTH) gsum = rd.template reduce<SumOp>(sum);
+    if (rank == 0 && t == 0) finish_item<KIND, T, SMOOTH>(a, r, cb, col0, gm, gs, gsum);
+  }
+  cl.sync();  // no CTA leaves while another may still read its exchange slots
+}
+
 namespace {
 
 inline int round_up32(int v) { return (v + 31) & ~31; }
@@ -388,6 +449,41 @@ cudaError_t launch_tma_stat(StatArgs a, cudaStream_t st) {
   return launch_tma_stat_v<KIND, T, SMOOTH, 4>(a, st, kTmaConsumers, kTmaStages);
 }
 
+// Cluster split for few long items: returns cudaErrorNotSupported when it
+// does not apply.
+template <int KIND, typename T, bool SMOOTH>
+cudaError_t launch_cluster_stat(StatArgs a, cudaStream_t st) {
+  constexpr int V = Elt<T>::kPerVec;
+  const int64_t items = a.M * a.nseg;
+  const int64_t nv = a.seg / V;  // vectors of a full item
+  // about 32 vectors per thread of a 512-thread CTA per slice
+  int64_t C = (nv + 32 * 512 - 1) / (32 * 512);
+  if (C < 2) C = 2;
+  if (C > 8) C = 8;
+  const int64_t slice_vecs = (nv + C - 1) / C;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(512);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(C * sm_count()));
+  int max_clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&max_clusters, cluster_stat_kernel<KIND, T, SMOOTH>, &cfg) != cudaSuccess ||
+      max_clusters < 1) {
+    cudaGetLastError();
+    max_clusters = static_cast<int>(sm_count() / C);
+  }
+  if (max_clusters < 1) max_clusters = 1;
+  const int64_t nclusters = items < max_clusters ? items : max_clusters;
+  cfg.gridDim = dim3(static_cast<unsigned>(nclusters * C));
+  return cudaLaunchKernelEx(&cfg, cluster_stat_kernel<KIND, T, SMOOTH>, a, slice_vecs);
+}
+
 template <int KIND, typename T, bool SMOOTH>
 cudaError_t dispatch_vec(StatArgs a, cudaStream_t st) {
   constexpr int E = Elt<T>::kPerVec;
@@ -402,6 +498,11 @@ cudaError_t dispatch_vec(StatArgs a, cudaStream_t st) {
   // Measured best on B200 for vocab-sized rows: next loads prefetched, one
   // exponential pair in four on the FMA pipe, registers bounded to three
   // CTAs per SM.
+  // Few long items (fewer than SMs, at least 256 KiB each): one cluster of
+  // CTAs per item instead of one CTA group.
+  const bool few_long = a.M * a.nseg < sm_count() && item_bytes >= 256 * 1024;
+  if (tma_ok && (path == DSLPG_PATH_CLUSTER || (path == DSLPG_PATH_AUTO && few_long)))
+    return launch_cluster_stat<KIND, T, SMOOTH>(a, st);
   if (vec && path != DSLPG_PATH_STREAM) return launch_stat<KIND, T, E, SMOOTH, 4, true, 4, 3>(a, st);
   return launch_stat<KIND, T, 1, SMOOTH>(a, st);
 }

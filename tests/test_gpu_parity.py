@@ -387,3 +387,21 @@ def test_mean_dtype_kwarg(din, dout):
 def test_argmax_flatten():
     x = randn((37, 91), torch.float16, gen(5))
     assert torch.equal(B.argmax(x.cuda(), None).cpu(), oracle.argmax(x, None))
+
+
+@pytest.mark.parametrize("bs", [131072, 65536, 300000])
+@pytest.mark.parametrize("smooth", [False, True])
+def test_cross_entropy_few_long_rows(bs, smooth):
+    """Few rows of long column blocks: the cluster-split path of the forward."""
+    g = gen(bs + 3)
+    r, c = 6, 300000
+    lg = randn((r, c), torch.bfloat16, g, std=2.0)
+    lb = torch.randint(0, c, (r,), generator=g, dtype=torch.int64)
+    lb[1] = -100
+    kw = dict(smoothing=0.1 if smooth else 0.0, logit_scale=1.0, lse_square_scale=1e-4, ignored_index=-100,
+              total_classes=c, class_start_idx=0, BLOCK_SIZE=bs, HAS_SMOOTHING=smooth, SPLIT=False)
+    out = B.cross_entropy_fwd(lg.cuda(), lb.cuda(), **kw)
+    ref = oracle.cross_entropy_fwd(lg, lb, **kw, valid_only=True)
+    nv = ref[0].numel()
+    for o, rr in zip(out, ref):
+        assert_parity(o.reshape(-1)[:nv], rr, torch.float32)
