@@ -75,3 +75,47 @@ def test_generator_rows_are_position_independent():
     full = workloads.make("softmax_fp16", rows=(0, 5000)).args[0]
     part = workloads.make("softmax_fp16", rows=(4000, 4100)).args[0]
     assert torch.equal(full[4000:4100].view(torch.int16), part.view(torch.int16))
+
+
+def _gather_worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from dslperfgap_b200 import sharded
+        from oracle import oracle
+        M = 13  # uneven blocks: 4 / 4 / 5
+        r0, r1 = sharded.shard_rows(M, rank, world)
+        wl = workloads.make("cross_entropy_bf16", seed=0, rows=(0, M))
+        logits, labels = wl.args[0][r0:r1], wl.args[1][r0:r1].clone()
+        if rank == 1:
+            labels[0] = -100
+        loss, _, _ = oracle.cross_entropy_fwd(logits, labels, **wl.kwargs, valid_only=True)
+        full = sharded.gather_rows(loss, None)
+        lab_full = sharded.gather_rows(labels, None)
+        mean = sharded.cross_entropy_mean(loss, labels, -100, None)
+        if rank == 0:
+            out_q.put((full, lab_full, mean))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_three_rank_gather_and_mean_loss():
+    from oracle import oracle
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    full, lab_full, mean = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    wl = workloads.make("cross_entropy_bf16", seed=0, rows=(0, 13))
+    labels = wl.args[1].clone()
+    labels[4] = -100  # rank 1's first row
+    ref, _, _ = oracle.cross_entropy_fwd(wl.args[0], labels, **wl.kwargs, valid_only=True)
+    assert torch.equal(full, ref)
+    assert torch.equal(lab_full, labels)
+    keep = labels != -100
+    assert abs(mean - ref[keep].double().mean().item()) < 1e-12
