@@ -14,6 +14,7 @@ from .cross_entropy.cuda_impl import cross_entropy_fwd, cross_entropy_bwd
 from .mean_reduction.cuda_impl import mean_reduction
 from .max_reduction.cuda_impl import max_reduction
 from .argmax.cuda_impl import argmax
+from .linear_activation.cuda_impl import kernel_ff
 
 __all__ = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy_fwd", "cross_entropy_bwd",
-           "mean_reduction", "max_reduction", "argmax"]
+           "mean_reduction", "max_reduction", "argmax", "kernel_ff"]

@@ -45,6 +45,8 @@ SIGNATURES = {
     "dslpg_mean_reduction": [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
     "dslpg_max_reduction": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "dslpg_argmax": [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
+    "dslpg_kernel_ff_workspace_bytes": [_c_i64, _c_i64, _vp],
+    "dslpg_kernel_ff": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_i64, _vp],
     "dslpg_version": [],
     "dslpg_set_kernel_path": [_c_int],
 }

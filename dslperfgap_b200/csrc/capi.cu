@@ -103,7 +103,7 @@ extern "C" int dslpg_set_kernel_path(int path) {
 }
 
 extern "C" unsigned int dslpg_take_wait_timeouts(void) {
-  return dslpg::take_wait_timeouts_rownorm() + dslpg::take_wait_timeouts_rowstat();
+  return dslpg::take_wait_timeouts_rownorm() + dslpg::take_wait_timeouts_rowstat() + dslpg::take_wait_timeouts_ff();
 }
 
 extern "C" int dslpg_version(void) { return (0 << 16) | 1; }

@@ -425,6 +425,7 @@ int kernel_path();
 // Per-file counters of bounded waits that ran out of time (read and reset).
 unsigned int take_wait_timeouts_rownorm();
 unsigned int take_wait_timeouts_rowstat();
+unsigned int take_wait_timeouts_ff();
 
 inline int dtype_size(int dt) { return dt == DSLPG_F32 ? 4 : 2; }
 inline bool is_float_dtype(int dt) { return dt == DSLPG_F32 || dt == DSLPG_F16 || dt == DSLPG_BF16; }

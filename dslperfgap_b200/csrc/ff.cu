@@ -1,0 +1,357 @@
+// ff.cu — Llama feed-forward with the RMSNorm fused around a tcgen05 dual
+// GEMM (sm_100a): ViperBench linear_activation.kernel_ff.
+//
+//   a_norm[m] = rsqrt(sum_k x[m,k]^2 / K + 1e-6)             (fp32)
+//   xs[m,k]   = x[m,k] * rms_w[k]                              (rounded to fp16)
+//   acc1 = xs @ w1^T, acc3 = xs @ w3^T                         (fp16 in, fp32 acc)
+//   out  = silu(a_norm * acc1) * (a_norm * acc3)               (stored as fp16)
+// (ViperBench/linear_activation/pytorch_impl.py:5-54.)
+//
+// Two kernels:
+//  * ff_prologue_kernel: one pass over x per row: a_norm and xs.
+//  * ff_gemm_kernel: one CTA per 128x128 output tile, warp-specialised:
+//      warp 0 (one lane)  TMA tensor loads of xs / w1 / w3 tiles (BK = 64,
+//                         128-byte swizzle) into a 4-stage shared-memory ring;
+//      warp 1             allocates 256 TMEM columns (acc1 | acc3), one lane
+//                         issues tcgen05.mma (M=128, N=128, K=16, fp16 -> fp32)
+//                         and tcgen05.commit releases each stage;
+//      warps 2-5          the epilogue: tcgen05.ld of both accumulators, the
+//                         a_norm scale, the SiLU gate, fp16 stores.
+// No TMA multicast; no peer memory. Every mbarrier wait is bounded (1 s of
+// %globaltimer); a wait that runs out records a device counter, the kernel
+// finishes its control flow without further waits or stores, the producer
+// drains its copies and the TMEM columns are freed before the CTA exits.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "pipe.cuh"
+
+namespace dslpg {
+
+static __device__ unsigned int g_ff_timeouts;
+
+constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
+constexpr uint32_t kTileA = kBM * kBK * 2;  // 16 KiB
+constexpr uint32_t kTileB = kBN * kBK * 2;  // 16 KiB
+constexpr uint32_t kStageBytes = kTileA + 2 * kTileB;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kFfThreads = 192;
+constexpr size_t kFfSmem = 1024 + kStages * kStageBytes + 1024;  // alignment + ring + barriers
+
+// ---------------------------------------------------------------- prologue
+// One CTA (256 threads) per row group, 16-byte vectors; K % 8 == 0.
+__global__ void __launch_bounds__(256) ff_prologue_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
+                                                          __half* __restrict__ xs, float* __restrict__ a_norm,
+                                                          int64_t M, int K) {
+  __shared__ float red[32];
+  const int nvec = K / 8;
+  for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
+    const __half* xr = x + m * K;
+    __half* yr = xs + m * K;
+    float ss = 0.f;
+    for (int j = threadIdx.x; j < nvec; j += blockDim.x) {
+      const Vec16 v = ld_stream(xr + static_cast<int64_t>(j) * 8);
+      const Vec16 wv = ld_keep(w + static_cast<int64_t>(j) * 8);
+      Vec16 o;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 a = *reinterpret_cast<const __half2*>(&v.w[i]);
+        const __half2 b = *reinterpret_cast<const __half2*>(&wv.w[i]);
+        const float2 af = __half22float2(a);
+        ss = fmaf(af.x, af.x, ss);
+        ss = fmaf(af.y, af.y, ss);
+        const __half2 p = __hmul2(a, b);  // x * rms_w in fp16, as the reference
+        o.w[i] = *reinterpret_cast<const uint32_t*>(&p);
+      }
+      st_stream(yr + static_cast<int64_t>(j) * 8, o);
+    }
+    ss = group_reduce<SumOp>(ss, red, blockDim.x >> 5, 0);
+    if (threadIdx.x == 0) a_norm[m] = rsqrtf(ss / static_cast<float>(K) + 1e-6f);
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ tcgen05
+// Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle
+// (rows of 64 fp16 = 128 bytes; 8-row atoms 1024 bytes apart): start address,
+// stride byte offset 1024, descriptor version 1, layout SWIZZLE_128B.
+DSLPG_DEV uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;            // leading byte offset (unused when swizzled)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;    // stride byte offset
+  d |= static_cast<uint64_t>(1u) << 46;            // version
+  d |= static_cast<uint64_t>(2u) << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, fp16 A and B, both
+// K-major, N = 128, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+
+DSLPG_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+DSLPG_DEV void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+DSLPG_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+#define DSLPG_R32(r) \
+  "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), \
+  "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),        \
+  "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),       \
+  "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes (one row per lane).
+DSLPG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%"
+      "20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : DSLPG_R32(r)
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct FfArgs {
+  const float* a_norm;
+  __half* out;
+  int64_t M, N;
+  int K;
+};
+
+__global__ void __launch_bounds__(kFfThreads, 1)
+    ff_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b1,
+                   const __grid_constant__ CUtensorMap map_b3, const FfArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t ring = (raw + 1023u) & ~1023u;  // 1024-aligned for the 128-byte swizzle atoms
+  const uint32_t bars = ring + kStages * kStageBytes;
+  const uint32_t full0 = bars, empty0 = bars + 8u * kStages, accum_bar = bars + 16u * kStages;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kBM;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kBN;
+  const int kblocks = (a.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    mbar_init(accum_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == 1) {  // TMEM for both accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    // ----------------------------------------------------------- producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % kStages;
+        const uint32_t ph = (kb / kStages) & 1u;
+        if (abort_flag) break;
+        if (kb >= kStages && !mbar_wait(empty0 + 8u * s, ph ^ 1u, kWaitLimitNs)) {
+          atomicAdd(&g_ff_timeouts, 1u);
+          abort_flag = 1;
+          break;
+        }
+        const uint32_t st = ring + static_cast<uint32_t>(s) * kStageBytes;
+        mbar_arrive_expect_tx(full0 + 8u * s, kStageBytes);
+        tma_load_2d(st, &map_a, kb * kBK, static_cast<int>(m0), full0 + 8u * s);
+        tma_load_2d(st + kTileA, &map_b1, kb * kBK, static_cast<int>(n0), full0 + 8u * s);
+        tma_load_2d(st + kTileA + kTileB, &map_b3, kb * kBK, static_cast<int>(n0), full0 + 8u * s);
+        ++issued;
+      }
+      // drain: no copy may still be landing when the CTA exits
+      for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; ++kb)
+        if (!mbar_wait(full0 + 8u * (kb % kStages), (kb / kStages) & 1u, kWaitLimitNs))
+          atomicAdd(&g_ff_timeouts, 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % kStages;
+        if (abort_flag) break;
+        if (!mbar_wait(full0 + 8u * s, (kb / kStages) & 1u, kWaitLimitNs)) {
+          atomicAdd(&g_ff_timeouts, 1u);
+          abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t st = ring + static_cast<uint32_t>(s) * kStageBytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {  // K = 16 per MMA: 32 bytes into the swizzled rows
+          const uint64_t ad = smem_desc_sw128(st + 32u * k);
+          const uint64_t b1 = smem_desc_sw128(st + kTileA + 32u * k);
+          const uint64_t b3 = smem_desc_sw128(st + kTileA + kTileB + 32u * k);
+          const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+          umma_f16(tmem, ad, b1, acc);
+          umma_f16(tmem + kBN, ad, b3, acc);
+        }
+        umma_commit(empty0 + 8u * s);  // the stage is free once these MMAs have read it
+      }
+      umma_commit(accum_bar);  // every MMA issued so far has completed
+      if (!mbar_wait(accum_bar, 0u, kWaitLimitNs)) atomicAdd(&g_ff_timeouts, 1u);
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    if (!mbar_wait(accum_bar, 0u, kWaitLimitNs)) {
+      atomicAdd(&g_ff_timeouts, 1u);
+      abort_flag = 1;
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int64_t m = m0 + 32 * q + lane;
+    const bool row_ok = m < a.M && !abort_flag;
+    const float an = row_ok ? a.a_norm[m] : 0.f;
+    for (int c = 0; c < kBN / 32; ++c) {
+      uint32_t r1[32], r3[32];
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * q) << 16);
+      tmem_ld32(lane_addr + 32u * c, r1);
+      tmem_ld32(lane_addr + kBN + 32u * c, r3);
+      if (!row_ok) continue;
+      const int64_t nb = n0 + 32 * c;
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float v[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float g = __uint_as_float(r1[2 * i + h]) * an;
+          const float u = __uint_as_float(r3[2 * i + h]) * an;
+          const float sig = 1.0f / (1.0f + ex2(-g * kLog2e));
+          v[h] = (g * sig) * u;
+        }
+        packed[i] = pack2<__half>(v[0], v[1]);
+      }
+      __half* orow = a.out + m * a.N;
+      if (nb + 32 <= a.N && (a.N % 8) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          st_stream(orow + nb + 8 * i, Vec16{{packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]}});
+      } else {
+        for (int i = 0; i < 32; ++i) {
+          if (nb + i >= a.N) break;
+          const uint32_t w = packed[i >> 1];
+          orow[nb + i] = __ushort_as_half(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xffffu)));
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ------------------------------------------------------------------- host
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// [rows, K] fp16 row-major, boxes of 128 rows x 64 columns, 128-byte swizzle,
+// zero fill out of bounds.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int K) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+  const cuuint32_t box[2] = {kBK, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+unsigned int take_wait_timeouts_ff() {
+  unsigned int v = 0, zero = 0;
+  cudaMemcpyFromSymbol(&v, g_ff_timeouts, sizeof(v));
+  cudaMemcpyToSymbol(g_ff_timeouts, &zero, sizeof(zero));
+  return v;
+}
+
+}  // namespace dslpg
+
+using namespace dslpg;
+
+extern "C" int dslpg_kernel_ff_workspace_bytes(int64_t M, int64_t K, int64_t* bytes) {
+  if (bytes == nullptr) return DSLPG_ERR_NULL_POINTER;
+  if (M < 0 || K < 0) return DSLPG_ERR_BAD_SHAPE;
+  // xs [M, K] fp16 (256-byte aligned), then a_norm [M] fp32
+  *bytes = ((M * K * 2 + 255) / 256) * 256 + M * 4;
+  return DSLPG_OK;
+}
+
+extern "C" int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, const void* rms_w, void* out,
+                               int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
+                               cudaStream_t stream) {
+  if (!x || !w1 || !w3 || !rms_w || !out || !workspace) return DSLPG_ERR_NULL_POINTER;
+  if (M < 0 || N < 0 || K <= 0 || K % 8 != 0 || K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff)
+    return DSLPG_ERR_BAD_SHAPE;
+  int64_t need = 0;
+  dslpg_kernel_ff_workspace_bytes(M, K, &need);
+  if (workspace_bytes < need) return DSLPG_ERR_BAD_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(w1, 16) || !aligned(w3, 16) || !aligned(rms_w, 16) || !aligned(out, 16) ||
+      !aligned(workspace, 256))
+    return DSLPG_ERR_BAD_ARGUMENT;
+  if (M == 0 || N == 0) return DSLPG_OK;
+  __half* xs = static_cast<__half*>(workspace);
+  float* a_norm = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((M * K * 2 + 255) / 256) * 256);
+
+  const int pgrid = persistent_grid(reinterpret_cast<const void*>(&ff_prologue_kernel), 256, 0, M);
+  ff_prologue_kernel<<<pgrid, 256, 0, stream>>>(static_cast<const __half*>(x), static_cast<const __half*>(rms_w), xs,
+                                                a_norm, M, static_cast<int>(K));
+  if (cudaError_t e = cudaGetLastError()) return static_cast<int>(e);
+
+  CUtensorMap ma, mb1, mb3;
+  if (!make_map(&ma, xs, M, static_cast<int>(K)) || !make_map(&mb1, w1, N, static_cast<int>(K)) ||
+      !make_map(&mb3, w3, N, static_cast<int>(K)))
+    return static_cast<int>(cudaErrorInvalidValue);
+  const void* fn = reinterpret_cast<const void*>(&ff_gemm_kernel);
+  if (cudaError_t e = allow_dynamic_smem(fn, kFfSmem)) return static_cast<int>(e);
+  FfArgs args{a_norm, static_cast<__half*>(out), M, N, static_cast<int>(K)};
+  const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN), static_cast<unsigned>((M + kBM - 1) / kBM));
+  ff_gemm_kernel<<<grid, kFfThreads, kFfSmem, stream>>>(ma, mb1, mb3, args);
+  return static_cast<int>(cudaGetLastError());
+}

@@ -194,6 +194,20 @@ DSLPG_API int dslpg_max_reduction(const void* x, void* values, int64_t* indices,
 DSLPG_API int dslpg_argmax(const void* x, int64_t* indices, int64_t M, int64_t N, int64_t K, int dtype,
                            cudaStream_t stream);
 
+/*
+ * Llama feed-forward with the RMSNorm fused around a tensor-core dual GEMM:
+ *   a_norm[m] = rsqrt(sum_k x[m,k]^2 / K + 1e-6);  xs = x * rms_w (fp16);
+ *   out[m,n] = silu(a_norm[m] * (xs @ w1^T)[m,n]) * (a_norm[m] * (xs @ w3^T)[m,n])   (fp16)
+ * x [M, K], w1 and w3 [N, K], rms_w [K], out [M, N]: all fp16, row-major,
+ * 16-byte aligned; K % 8 == 0. `workspace` (256-byte aligned) holds xs and
+ * a_norm: at least dslpg_kernel_ff_workspace_bytes(M, K) bytes.
+ * Replaces kernel_ff(x, w1, w3, rms_w) of ViperBench/linear_activation/pytorch_impl.py:5-54.
+ */
+DSLPG_API int dslpg_kernel_ff_workspace_bytes(int64_t M, int64_t K, int64_t* bytes);
+DSLPG_API int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, const void* rms_w, void* out,
+                              int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
+                              cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

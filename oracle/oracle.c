@@ -28,6 +28,7 @@
 #include <stdint.h>
 #include <string.h>
 #include <pthread.h>
+#include <stdlib.h>
 #include <unistd.h>
 
 enum { F32 = 0, F16 = 1, BF16 = 2, I32 = 3, I64 = 4 };
@@ -454,6 +455,49 @@ void oracle_max_reduction(const void* x, void* values, int64_t* indices, int64_t
   memset(&a, 0, sizeof(a));
   a.x = x; a.y = values; a.idx = indices; a.M = M; a.N = N; a.K = K; a.idt = dt; a.want_vals = values != 0;
   parallel_for(M * K, max_cols, &a);
+}
+
+/*
+ * kernel_ff of ViperBench/linear_activation/pytorch_impl.py:5-54 (fp16 in/out):
+ * a_norm = 1/sqrt(sum(x^2)/K + 1e-6); xs = fp16(x * rms_w); acc1 = xs @ w1^T,
+ * acc3 = xs @ w3^T (double here); out = fp16((acc1 * a) * sigmoid(acc1 * a) * (acc3 * a)).
+ */
+typedef struct {
+  const uint16_t *x, *w1, *w3, *rw;
+  uint16_t* out;
+  int64_t M, N, K;
+} ff_t;
+
+static void ff_rows(const void* ctx, int64_t m0, int64_t m1) {
+  const ff_t* a = (const ff_t*)ctx;
+  const int64_t K = a->K;
+  double* xs = (double*)malloc(sizeof(double) * (size_t)K);
+  if (!xs) return;
+  for (int64_t m = m0; m < m1; ++m) {
+    double ss = 0.0;
+    for (int64_t k = 0; k < K; ++k) {
+      const double v = half_to_float(a->x[m * K + k]);
+      ss += v * v;
+      xs[k] = half_to_float(float_to_half((float)(v * half_to_float(a->rw[k]))));
+    }
+    const double an = 1.0 / sqrt(ss / (double)K + 1e-6);
+    for (int64_t n = 0; n < a->N; ++n) {
+      double acc1 = 0.0, acc3 = 0.0;
+      for (int64_t k = 0; k < K; ++k) {
+        acc1 += xs[k] * half_to_float(a->w1[n * K + k]);
+        acc3 += xs[k] * half_to_float(a->w3[n * K + k]);
+      }
+      const double g = acc1 * an, u = acc3 * an;
+      a->out[m * a->N + n] = float_to_half((float)(g / (1.0 + exp(-g)) * u));
+    }
+  }
+  free(xs);
+}
+
+void oracle_kernel_ff(const uint16_t* x, const uint16_t* w1, const uint16_t* w3, const uint16_t* rms_w,
+                      uint16_t* out, int64_t M, int64_t N, int64_t K) {
+  ff_t a = {x, w1, w3, rms_w, out, M, N, K};
+  parallel_for(M, ff_rows, &a);
 }
 
 /* Bit-level conversions, exported so tests can check them. */

@@ -59,6 +59,7 @@ def lib() -> ctypes.CDLL:
                                                        i64, cd, i64, ci]
                 l.oracle_mean_reduction.argtypes = [vp, vp, i64, i64, i64, ci, ci]
                 l.oracle_max_reduction.argtypes = [vp, vp, vp, i64, i64, i64, ci]
+                l.oracle_kernel_ff.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64]
                 l.oracle_set_threads.argtypes = [ci]
                 l.oracle_max_threads.restype = ci
                 l.oracle_half_to_float.argtypes = [ctypes.c_uint16]
@@ -246,3 +247,13 @@ def argmax(input_tensor, dim, keepdim=False):
     i = torch.empty(os_, dtype=torch.int64)
     lib().oracle_max_reduction(xc.data_ptr(), None, i.data_ptr(), m, n, k, _code(x))
     return i
+
+
+def kernel_ff(x, w1, w3, rms_w):
+    """ViperBench/linear_activation/pytorch_impl.py:5-54: fp16 [batch, seq, n_out]."""
+    x, w1, w3, rms_w = (_host(t.half() if t.dtype != torch.float16 else t) for t in (x, w1, w3, rms_w))
+    b, s, k = x.shape
+    n = w1.shape[0]
+    out = torch.empty((b, s, n), dtype=torch.float16)
+    lib().oracle_kernel_ff(x.data_ptr(), w1.data_ptr(), w3.data_ptr(), rms_w.data_ptr(), out.data_ptr(), b * s, n, k)
+    return out

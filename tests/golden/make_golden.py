@@ -37,7 +37,7 @@ HERE = Path(__file__).resolve().parent
 REF = Path(os.environ.get("DSLPG_REFERENCE", "/root/reference")) / "ViperBench"
 
 OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd",
-       "mean_reduction", "max_reduction", "argmax"]
+       "mean_reduction", "max_reduction", "argmax", "linear_activation"]
 
 
 def load_ref(kernel: str):
@@ -332,7 +332,28 @@ def cases_argmax():
     return _argmax_inputs()
 
 
+def cases_linear_activation():
+    c = []
+    g42 = torch.Generator().manual_seed(42)  # the reference test's seed (test.py:10), CPU generator
+    for b, s_, d in [(2, 4, 64), (3, 4, 64), (2, 8, 64), (1, 16, 128)]:  # test.py:21-26 (n_out = dim)
+        x = torch.randn((b, s_, d), generator=g42).half()
+        w1 = torch.randn((d, d), generator=g42).half()
+        w3 = torch.randn((d, d), generator=g42).half()
+        rw = torch.randn((d,), generator=g42).half()
+        c.append((f"ref_{b}x{s_}x{d}", [x, w1, w3, rw], {}))
+    for name, (b, s_, d, n) in [("ragged_1x70x256_n200", (1, 70, 256, 200)), ("multi_tile_2x96x512_n384", (2, 96, 512, 384)),
+                                ("k_tail_1x130x1000_n136", (1, 130, 1000, 136))]:
+        x = randn(b, s_, d, dtype=torch.float16)
+        w1 = randn(n, d, std=0.05, dtype=torch.float16)
+        w3 = randn(n, d, std=0.05, dtype=torch.float16)
+        rw = randn(d, mean=1.0, std=0.1, dtype=torch.float16)
+        c.append((name, [x, w1, w3, rw], {}))
+    return c
+
+
 def call(op, mod, args, kwargs):
+    if op == "linear_activation":
+        return mod.kernel_ff(*args)
     if op in ("mean_reduction", "max_reduction", "argmax"):
         kw = dict(kwargs)
         if "dtype" in kw:
@@ -367,7 +388,7 @@ def main() -> int:
     builders = dict(layer_norm=cases_layer_norm, rms_norm=cases_rms_norm, softmax=cases_softmax,
                     log_softmax=cases_log_softmax, logsumexp=cases_logsumexp, cross_entropy=cases_cross_entropy,
                     cross_entropy_bwd=cases_cross_entropy_bwd, mean_reduction=cases_mean_reduction,
-                    max_reduction=cases_max_reduction, argmax=cases_argmax)
+                    max_reduction=cases_max_reduction, argmax=cases_argmax, linear_activation=cases_linear_activation)
     total = 0
     for op in OPS:
         mod = load_ref(op)
