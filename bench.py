@@ -96,6 +96,19 @@ def measured_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_tensor_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured cuBLAS bf16, burst"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+TENSOR_PEAK = measured_tensor_peak()
+
+
 def profile_traffic():
     """DRAM bytes per launch from a committed ncu summary, if present."""
     p = ROOT / "profiles" / "traffic.json"
@@ -275,6 +288,16 @@ def direct_launcher(wl, dev):
             f = lambda: lib.dslpg_max_reduction(x.data_ptr(), vals.data_ptr(), idx.data_ptr(), M, N, 1, code, stream)
         else:
             f = lambda: lib.dslpg_argmax(x.data_ptr(), idx.data_ptr(), M, N, 1, code, stream)
+    elif cfg.op == "linear_activation":
+        import ctypes
+        x, w1, w3, rw = a
+        y = torch.empty((M, cfg.N), dtype=torch.float16, device=dev)
+        need = ctypes.c_int64(0)
+        lib.dslpg_kernel_ff_workspace_bytes(M, cfg.K, ctypes.byref(need))
+        ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+        keep = [y, ws]
+        f = lambda: lib.dslpg_kernel_ff(x.data_ptr(), w1.data_ptr(), w3.data_ptr(), rw.data_ptr(), y.data_ptr(), M,
+                                        cfg.N, cfg.K, ws.data_ptr(), need.value, stream)
     elif cfg.op == "cross_entropy_bwd":
         k = wl.kwargs
         dloss, x, lse, labels = a
@@ -311,6 +334,18 @@ def torch_baseline(wl):
         return "torch.logsumexp", lambda: torch.logsumexp(a[0], -1)
     if cfg.op == "cross_entropy":
         return "F.cross_entropy(mean)", lambda: F.cross_entropy(a[0], a[1], ignore_index=-100)
+    if cfg.op == "linear_activation":
+        # the same computation with cuBLAS fp16 GEMMs (the reference's own
+        # pytorch_impl upcasts to fp32 matmuls; that is timed separately)
+        import torch.nn.functional as F
+        x, w1, w3, rw = a
+
+        def ff():
+            xf = x.reshape(-1, cfg.K)
+            an = torch.rsqrt(xf.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+            xs = xf * rw
+            return (F.silu((xs @ w1.t()).float() * an) * ((xs @ w3.t()).float() * an)).half()
+        return "torch fp16 GEMMs (cuBLAS) + eager epilogue", ff
     if cfg.op == "mean_reduction":
         return "torch.mean", lambda: torch.mean(a[0], 1)
     if cfg.op == "max_reduction":
@@ -360,14 +395,22 @@ def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler
     agg_gbs = total_bytes / (t_max * 1e-3) / 1e9
     kernel_ms = statistics.mean(per)
     achieved = bytes_rank / (kernel_ms * 1e-3) / 1e9
-    res = {
+    res = {}
+    flops = workloads.algo_flops(cfg, wl.M)
+    if flops:
+        tf = flops / (kernel_ms * 1e-3) / 1e12
+        res["tflops_per_gpu"] = round(tf, 1)
+        res["frac_tensor_measured"] = round(tf / TENSOR_PEAK[0], 4)
+        res["tensor_peak"] = f"{TENSOR_PEAK[0]} TFLOP/s ({TENSOR_PEAK[1]})"
+        res["algo_flops_per_launch"] = flops
+    res.update({
         "shape": [wl.M, cfg.N], "dtype": SHORT[cfg.dtype], "rows_per_gpu": wl.M,
         "scaling": "strong" if sharded else "weak",
         "ms_per_step": round(ms_step, 5), "median_ms": round(statistics.median(per), 5),
         "gbs": round(agg_gbs, 1), "gbs_per_gpu": round(achieved, 1),
         "frac_measured": round(achieved / peak, 4), "frac_spec": round(achieved / SPEC_HBM_GBS, 4),
         "algo_bytes_per_launch": bytes_rank, "launches": steps,
-    }
+    })
     if with_torch:
         label, fn = torch_baseline(wl)
         try:

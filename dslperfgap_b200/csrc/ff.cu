@@ -9,19 +9,24 @@
 //
 // Two kernels:
 //  * ff_prologue_kernel: one pass over x per row: a_norm and xs.
-//  * ff_gemm_kernel: one CTA per 128x128 output tile, warp-specialised:
+//  * ff_gemm_kernel: persistent, one CTA per SM walking 128x128 output tiles,
+//    warp-specialised:
 //      warp 0 (one lane)  TMA tensor loads of xs / w1 / w3 tiles (BK = 64,
 //                         128-byte swizzle) into a 4-stage shared-memory ring;
-//      warp 1             allocates 256 TMEM columns (acc1 | acc3), one lane
-//                         issues tcgen05.mma (M=128, N=128, K=16, fp16 -> fp32)
-//                         and tcgen05.commit releases each stage;
+//      warp 1             allocates all 512 TMEM columns: two buffers of
+//                         (acc1 | acc3); one lane issues tcgen05.mma (M=128,
+//                         N=128, K=16, fp16 -> fp32), tcgen05.commit releases
+//                         each stage and hands a finished buffer to the epilogue;
 //      warps 2-5          the epilogue: tcgen05.ld of both accumulators, the
-//                         a_norm scale, the SiLU gate, fp16 stores.
+//                         a_norm scale, the SiLU gate, fp16 stores — while the
+//                         MMAs of the next tile run into the other buffer.
 // No TMA multicast; no peer memory. Every mbarrier wait is bounded (1 s of
 // %globaltimer); a wait that runs out records a device counter, the kernel
 // finishes its control flow without further waits or stores, the producer
 // drains its copies and the TMEM columns are freed before the CTA exits.
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "pipe.cuh"
@@ -34,7 +39,7 @@ constexpr int kBM = 128, kBN = 128, kBK = 64, kStages = 4;
 constexpr uint32_t kTileA = kBM * kBK * 2;  // 16 KiB
 constexpr uint32_t kTileB = kBN * kBK * 2;  // 16 KiB
 constexpr uint32_t kStageBytes = kTileA + 2 * kTileB;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;  // two buffers of (acc1 | acc3), 128 columns each
 constexpr uint32_t kFfThreads = 192;
 constexpr size_t kFfSmem = 1024 + kStages * kStageBytes + 1024;  // alignment + ring + barriers
 
@@ -128,6 +133,19 @@ struct FfArgs {
   int K;
 };
 
+// Tile order of the persistent grid: groups of up to kGroupM row tiles; inside
+// a group the row tile varies fastest, so the CTAs running at one time share a
+// few weight tiles (read from DRAM once) and the group's xs rows stay in L2.
+constexpr int kGroupM = 16;
+
+DSLPG_DEV void tile_coords(int t, int mt, int nt, int& tm, int& tn) {
+  const int per_group = kGroupM * nt;
+  const int g = t / per_group, r = t - g * per_group;
+  const int gm = min(kGroupM, mt - g * kGroupM);
+  tm = g * kGroupM + r % gm;
+  tn = r / gm;
+}
+
 __global__ void __launch_bounds__(kFfThreads, 1)
     ff_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b1,
                    const __grid_constant__ CUtensorMap map_b3, const FfArgs a) {
@@ -138,9 +156,12 @@ __global__ void __launch_bounds__(kFfThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t ring = (raw + 1023u) & ~1023u;  // 1024-aligned for the 128-byte swizzle atoms
   const uint32_t bars = ring + kStages * kStageBytes;
-  const uint32_t full0 = bars, empty0 = bars + 8u * kStages, accum_bar = bars + 16u * kStages;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kBM;
-  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kBN;
+  // full[s], empty[s]: the stage ring; tfull[b], tempty[b]: the two TMEM
+  // accumulator buffers; done: every MMA issued has completed.
+  const uint32_t full0 = bars, empty0 = bars + 8u * kStages;
+  const uint32_t tfull0 = bars + 16u * kStages, tempty0 = tfull0 + 16u, done_bar = tfull0 + 32u;
+  const int mt = static_cast<int>((a.M + kBM - 1) / kBM), nt = static_cast<int>((a.N + kBN - 1) / kBN);
+  const int tiles = mt * nt;
   const int kblocks = (a.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -148,11 +169,15 @@ __global__ void __launch_bounds__(kFfThreads, 1)
       mbar_init(full0 + 8u * s, 1);
       mbar_init(empty0 + 8u * s, 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8u * b, 1);
+      mbar_init(tempty0 + 8u * b, 4);  // one arrival per epilogue warp
+    }
+    mbar_init(done_bar, 1);
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == 1) {  // TMEM for both accumulators
+  if (warp == 1) {  // TMEM: two buffers of (acc1 | acc3)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -165,97 +190,124 @@ __global__ void __launch_bounds__(kFfThreads, 1)
   if (warp == 0) {
     // ----------------------------------------------------------- producer
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (kb / kStages) & 1u;
-        if (abort_flag) break;
-        if (kb >= kStages && !mbar_wait(empty0 + 8u * s, ph ^ 1u, kWaitLimitNs)) {
-          atomicAdd(&g_ff_timeouts, 1u);
-          abort_flag = 1;
-          break;
+      uint32_t it = 0;  // stage uses issued so far
+      for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, mt, nt, tm, tn);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+          if (abort_flag) break;
+          if (it >= kStages && !mbar_wait(empty0 + 8u * s, ph ^ 1u, kWaitLimitNs)) {
+            atomicAdd(&g_ff_timeouts, 1u);
+            abort_flag = 1;
+            break;
+          }
+          const uint32_t st = ring + s * kStageBytes;
+          mbar_arrive_expect_tx(full0 + 8u * s, kStageBytes);
+          tma_load_2d(st, &map_a, kb * kBK, tm * kBM, full0 + 8u * s);
+          tma_load_2d(st + kTileA, &map_b1, kb * kBK, tn * kBN, full0 + 8u * s);
+          tma_load_2d(st + kTileA + kTileB, &map_b3, kb * kBK, tn * kBN, full0 + 8u * s);
         }
-        const uint32_t st = ring + static_cast<uint32_t>(s) * kStageBytes;
-        mbar_arrive_expect_tx(full0 + 8u * s, kStageBytes);
-        tma_load_2d(st, &map_a, kb * kBK, static_cast<int>(m0), full0 + 8u * s);
-        tma_load_2d(st + kTileA, &map_b1, kb * kBK, static_cast<int>(n0), full0 + 8u * s);
-        tma_load_2d(st + kTileA + kTileB, &map_b3, kb * kBK, static_cast<int>(n0), full0 + 8u * s);
-        ++issued;
       }
       // drain: no copy may still be landing when the CTA exits
-      for (int kb = (issued > kStages ? issued - kStages : 0); kb < issued; ++kb)
-        if (!mbar_wait(full0 + 8u * (kb % kStages), (kb / kStages) & 1u, kWaitLimitNs))
-          atomicAdd(&g_ff_timeouts, 1u);
+      for (uint32_t u = (it > kStages ? it - kStages : 0); u < it; ++u)
+        if (!mbar_wait(full0 + 8u * (u % kStages), (u / kStages) & 1u, kWaitLimitNs)) atomicAdd(&g_ff_timeouts, 1u);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kStages;
-        if (abort_flag) break;
-        if (!mbar_wait(full0 + 8u * s, (kb / kStages) & 1u, kWaitLimitNs)) {
+      uint32_t it = 0, j = 0;
+      for (int t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++j) {
+        const uint32_t b = j & 1u;
+        if (j >= 2 && !mbar_wait(tempty0 + 8u * b, ((j >> 1) & 1u) ^ 1u, kWaitLimitNs)) {
           atomicAdd(&g_ff_timeouts, 1u);
           abort_flag = 1;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t st = ring + static_cast<uint32_t>(s) * kStageBytes;
+        const uint32_t acc_base = tmem + b * 2u * kBN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (abort_flag) break;
+          if (!mbar_wait(full0 + 8u * s, (it / kStages) & 1u, kWaitLimitNs)) {
+            atomicAdd(&g_ff_timeouts, 1u);
+            abort_flag = 1;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = ring + s * kStageBytes;
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {  // K = 16 per MMA: 32 bytes into the swizzled rows
-          const uint64_t ad = smem_desc_sw128(st + 32u * k);
-          const uint64_t b1 = smem_desc_sw128(st + kTileA + 32u * k);
-          const uint64_t b3 = smem_desc_sw128(st + kTileA + kTileB + 32u * k);
-          const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-          umma_f16(tmem, ad, b1, acc);
-          umma_f16(tmem + kBN, ad, b3, acc);
+          for (int k = 0; k < kBK / 16; ++k) {  // K = 16 per MMA: 32 bytes into the swizzled rows
+            const uint64_t ad = smem_desc_sw128(st + 32u * k);
+            const uint64_t b1 = smem_desc_sw128(st + kTileA + 32u * k);
+            const uint64_t b3 = smem_desc_sw128(st + kTileA + kTileB + 32u * k);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_f16(acc_base, ad, b1, acc);
+            umma_f16(acc_base + kBN, ad, b3, acc);
+          }
+          umma_commit(empty0 + 8u * s);  // the stage is free once these MMAs have read it
         }
-        umma_commit(empty0 + 8u * s);  // the stage is free once these MMAs have read it
+        umma_commit(tfull0 + 8u * b);  // the tile's accumulators are complete
       }
-      umma_commit(accum_bar);  // every MMA issued so far has completed
-      if (!mbar_wait(accum_bar, 0u, kWaitLimitNs)) atomicAdd(&g_ff_timeouts, 1u);
+      umma_commit(done_bar);  // every MMA issued so far has completed
+      if (!mbar_wait(done_bar, 0u, kWaitLimitNs)) atomicAdd(&g_ff_timeouts, 1u);
     }
     __syncwarp();
   } else {
     // ----------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
-    if (!mbar_wait(accum_bar, 0u, kWaitLimitNs)) {
-      atomicAdd(&g_ff_timeouts, 1u);
-      abort_flag = 1;
-    }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int64_t m = m0 + 32 * q + lane;
-    const bool row_ok = m < a.M && !abort_flag;
-    const float an = row_ok ? a.a_norm[m] : 0.f;
-    for (int c = 0; c < kBN / 32; ++c) {
-      uint32_t r1[32], r3[32];
-      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * q) << 16);
-      tmem_ld32(lane_addr + 32u * c, r1);
-      tmem_ld32(lane_addr + kBN + 32u * c, r3);
-      if (!row_ok) continue;
-      const int64_t nb = n0 + 32 * c;
-      uint32_t packed[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float v[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float g = __uint_as_float(r1[2 * i + h]) * an;
-          const float u = __uint_as_float(r3[2 * i + h]) * an;
-          const float sig = 1.0f / (1.0f + ex2(-g * kLog2e));
-          v[h] = (g * sig) * u;
-        }
-        packed[i] = pack2<__half>(v[0], v[1]);
+    uint32_t j = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      if (abort_flag) break;
+      const uint32_t b = j & 1u;
+      if (!mbar_wait(tfull0 + 8u * b, (j >> 1) & 1u, kWaitLimitNs)) {
+        atomicAdd(&g_ff_timeouts, 1u);
+        abort_flag = 1;
+        break;
       }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int tm, tn;
+      tile_coords(t, mt, nt, tm, tn);
+      const int64_t m = static_cast<int64_t>(tm) * kBM + 32 * q + lane;
+      const int64_t n0 = static_cast<int64_t>(tn) * kBN;
+      const bool row_ok = m < a.M;
+      const float an = row_ok ? a.a_norm[m] : 0.f;
+      const uint32_t lane_addr = tmem + b * 2u * kBN + (static_cast<uint32_t>(32 * q) << 16);
       __half* orow = a.out + m * a.N;
-      if (nb + 32 <= a.N && (a.N % 8) == 0) {
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r1[32], r3[32];
+        tmem_ld32(lane_addr + 32u * c, r1);
+        tmem_ld32(lane_addr + kBN + 32u * c, r3);
+        if (c == kBN / 32 - 1) {  // both accumulators read: hand the buffer back to the MMA warp
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty0 + 8u * b);
+        }
+        if (!row_ok) continue;
+        const int64_t nb = n0 + 32 * c;
+        uint32_t packed[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          st_stream(orow + nb + 8 * i, Vec16{{packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]}});
-      } else {
-        for (int i = 0; i < 32; ++i) {
-          if (nb + i >= a.N) break;
-          const uint32_t w = packed[i >> 1];
-          orow[nb + i] = __ushort_as_half(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xffffu)));
+        for (int i = 0; i < 16; ++i) {
+          float v[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float g = __uint_as_float(r1[2 * i + h]) * an;
+            const float u = __uint_as_float(r3[2 * i + h]) * an;
+            const float sig = 1.0f / (1.0f + ex2(-g * kLog2e));
+            v[h] = (g * sig) * u;
+          }
+          packed[i] = pack2<__half>(v[0], v[1]);
+        }
+        if (nb + 32 <= a.N && (a.N % 8) == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            st_stream(orow + nb + 8 * i, Vec16{{packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]}});
+        } else {
+          for (int i = 0; i < 32; ++i) {
+            if (nb + i >= a.N) break;
+            const uint32_t w = packed[i >> 1];
+            orow[nb + i] = __ushort_as_half(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xffffu)));
+          }
         }
       }
     }
@@ -351,7 +403,9 @@ extern "C" int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, co
   const void* fn = reinterpret_cast<const void*>(&ff_gemm_kernel);
   if (cudaError_t e = allow_dynamic_smem(fn, kFfSmem)) return static_cast<int>(e);
   FfArgs args{a_norm, static_cast<__half*>(out), M, N, static_cast<int>(K)};
-  const dim3 grid(static_cast<unsigned>((N + kBN - 1) / kBN), static_cast<unsigned>((M + kBM - 1) / kBM));
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+  if (tiles > 0x7fffffff) return DSLPG_ERR_BAD_SHAPE;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));  // one CTA per SM (TMEM: all 512 columns)
   ff_gemm_kernel<<<grid, kFfThreads, kFfSmem, stream>>>(ma, mb1, mb3, args);
   return static_cast<int>(cudaGetLastError());
 }

@@ -39,6 +39,7 @@ class Config:
     dtype: torch.dtype
     description: str
     kwargs: dict = field(default_factory=dict)
+    K: int = 0  # linear_activation: the reduction (model) dimension
 
 
 CONFIGS = {
@@ -74,6 +75,10 @@ CONFIGS = {
                "max (values, indices) over dim 1, fp16 x[8192,32768]~N(0,1) (benchmark.py:278-280)", {"dim": 1}),
         Config("argmax_fp16", "argmax", "argmax", 8192, 32768, torch.float16,
                "argmax over dim 1, fp16 x[8192,32768]~N(0,1) (benchmark.py:97-99)", {"dim": 1}),
+        Config("linear_activation_fp16", "linear_activation", "kernel_ff", 2048, 16384, torch.float16,
+               "Llama FFN kernel_ff fp16: x[1,2048,4096], w1/w3[16384,4096], rms_w[4096] ~N(0,1) "
+               "(the reference's large shape, benchmark.py:223-228); RMSNorm + dual GEMM + SiLU gate",
+               {}, K=4096),
         Config("layer_norm_bf16_sharded", "layer_norm", "layer_norm", 131072, 8192, torch.bfloat16,
                "row-sharded LayerNorm bf16 x[131072,8192]~N(0,1), w~N(1,0.1), b~N(0,0.1), eps=1e-5, "
                "row blocks over 1/2/4/8 GPUs", {"eps": 1e-5}),
@@ -147,7 +152,14 @@ def algo_bytes(cfg: Config, rows: int) -> int:
         return rows * cfg.N * es + rows * (es + 8)
     if cfg.op == "argmax":
         return rows * cfg.N * es + rows * 8
+    if cfg.op == "linear_activation":  # x, w1, w3, rms_w read once, out written once
+        return es * (rows * cfg.K + 2 * cfg.N * cfg.K + cfg.K + rows * cfg.N)
     raise KeyError(cfg.op)
+
+
+def algo_flops(cfg: Config, rows: int) -> int:
+    """Tensor-core work of linear_activation: two [rows, K] x [K, N] products."""
+    return 4 * rows * cfg.N * cfg.K if cfg.op == "linear_activation" else 0
 
 
 def shard_rows(M: int, rank: int, world: int) -> tuple:
@@ -209,6 +221,13 @@ def make(name: str, seed: int = 0, device="cpu", rows: tuple | None = None) -> W
         args = [_rows(cfg, r0, r1, seed, device, 3.0, True)]
     elif cfg.op == "logsumexp":
         args = [_rows(cfg, r0, r1, seed, device, 2.0, False)]
+    elif cfg.op == "linear_activation":
+        x = _rows(Config(cfg.name, cfg.op, cfg.fn_name, cfg.M, cfg.K, cfg.dtype, ""), r0, r1, seed, device, 1.0, False)
+        wcfg = Config(cfg.name, cfg.op, cfg.fn_name, cfg.N, cfg.K, cfg.dtype, "")
+        w1 = _rows(wcfg, 0, cfg.N, seed + 201, device, 1.0, False)
+        w3 = _rows(wcfg, 0, cfg.N, seed + 202, device, 1.0, False)
+        rw = _vec(cfg.K, cfg.dtype, seed + 203, device, 0.0, 1.0)
+        args = [x.reshape(1, r1 - r0, cfg.K), w1, w3, rw]
     elif cfg.op in ("mean_reduction", "max_reduction", "argmax"):
         args = [_rows(cfg, r0, r1, seed, device, 1.0, False)]
     elif cfg.op in ("cross_entropy", "cross_entropy_bwd"):
