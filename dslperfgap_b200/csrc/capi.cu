@@ -116,6 +116,9 @@ extern "C" const char* dslpg_error_string(int code) {
     case DSLPG_ERR_BAD_DTYPE: return "dslpg: unsupported dtype code";
     case DSLPG_ERR_BAD_EPS: return "dslpg: eps must be finite and >= 0";
     case DSLPG_ERR_BAD_ARGUMENT: return "dslpg: invalid argument";
+    case DSLPG_ERR_TOO_LARGE:
+      return "dslpg: problem too large for dslpg_kernel_ff_static's static scratch "
+             "(dslpg_kernel_ff_workspace_bytes(M, K) must be <= 16 MiB + 64 KiB); use dslpg_kernel_ff";
     default: break;
   }
   if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));

@@ -27,6 +27,8 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 
 #include "common.cuh"
 #include "pipe.cuh"
@@ -408,4 +410,56 @@ extern "C" int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, co
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));  // one CTA per SM (TMEM: all 512 columns)
   ff_gemm_kernel<<<grid, kFfThreads, kFfSmem, stream>>>(ma, mb1, mb3, args);
   return static_cast<int>(cudaGetLastError());
+}
+
+// ------------------------------------------------------ static-scratch entry
+// dslpg_kernel_ff for callers that cannot allocate device memory per call (a
+// C / FFI host with no device allocator of its own, or a loop that must not
+// pay cudaMalloc / cudaFree's device-wide synchronisation). xs and a_norm go to
+// this file-scope scratch instead of a caller workspace; nothing in it must
+// start at zero, since the prologue writes every byte the GEMM reads. One
+// scratch per device: overlapping calls on a device race on it.
+namespace dslpg {
+namespace {
+constexpr int64_t kStaticScratchBytes = DSLPG_KERNEL_FF_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_ff_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_scratch_addr[kMaxDevices];
+std::mutex g_scratch_mu;
+
+// The scratch's device address on the current device, looked up once per
+// device (with that device current) by the first call there.
+cudaError_t static_scratch(void** out) {
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    p = g_scratch_addr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      if (cudaError_t e = cudaGetSymbolAddress(&p, g_ff_scratch)) return e;
+      g_scratch_addr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return cudaSuccess;
+}
+}  // namespace
+}  // namespace dslpg
+
+extern "C" int dslpg_kernel_ff_static(const void* x, const void* w1, const void* w3, const void* rms_w, void* out,
+                                      int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (!x || !w1 || !w3 || !rms_w || !out) return DSLPG_ERR_NULL_POINTER;
+  if (M < 0 || N < 0 || K <= 0 || K % 8 != 0 || K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff)
+    return DSLPG_ERR_BAD_SHAPE;
+  if (M > 0 && K > kStaticScratchBytes / (2 * M)) return DSLPG_ERR_TOO_LARGE;  // before M * K can overflow
+  int64_t need = 0;
+  dslpg_kernel_ff_workspace_bytes(M, K, &need);
+  if (need > kStaticScratchBytes) return DSLPG_ERR_TOO_LARGE;
+  if (M == 0 || N == 0) return DSLPG_OK;
+  void* scratch = nullptr;
+  if (cudaError_t e = static_scratch(&scratch)) return static_cast<int>(e);
+  return dslpg_kernel_ff(x, w1, w3, rms_w, out, M, N, K, scratch, kStaticScratchBytes, stream);
 }

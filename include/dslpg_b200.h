@@ -53,7 +53,8 @@ enum {
   DSLPG_ERR_BAD_SHAPE = -2,
   DSLPG_ERR_BAD_DTYPE = -3,
   DSLPG_ERR_BAD_EPS = -4,
-  DSLPG_ERR_BAD_ARGUMENT = -5
+  DSLPG_ERR_BAD_ARGUMENT = -5,
+  DSLPG_ERR_TOO_LARGE = -6 /* dslpg_kernel_ff_static: the problem does not fit its static scratch */
 };
 
 /* Kernel-shape selection (normally DSLPG_PATH_AUTO; the others exist so tests
@@ -207,6 +208,30 @@ DSLPG_API int dslpg_kernel_ff_workspace_bytes(int64_t M, int64_t K, int64_t* byt
 DSLPG_API int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, const void* rms_w, void* out,
                               int64_t M, int64_t N, int64_t K, void* workspace, int64_t workspace_bytes,
                               cudaStream_t stream);
+
+/*
+ * dslpg_kernel_ff without a caller-provided workspace and without any device
+ * allocation: xs and a_norm live in a file-scope static __device__ scratch of
+ * DSLPG_KERNEL_FF_STATIC_SCRATCH_BYTES (16 MiB + 64 KiB), enough for
+ * M * K <= 8,388,608 fp16 elements (e.g. 2048 x 4096) as measured by
+ * dslpg_kernel_ff_workspace_bytes; larger problems return DSLPG_ERR_TOO_LARGE
+ * before anything is launched. It is meant for callers that cannot allocate
+ * device memory per call: a C / FFI host that owns no device allocator (the
+ * memory belongs to another framework's pool), or a loop where the device-wide
+ * synchronisation of cudaMalloc / cudaFree is not acceptable.
+ * Set-up: the first call on each device (the device current at the call) looks
+ * up the scratch address with cudaGetSymbolAddress, which may load this
+ * library's device code; make that first call before any stream capture.
+ * No part of the scratch has to start at zero (every call writes all of xs and
+ * a_norm before reading them). There is ONE scratch per device: calls that
+ * overlap on the same device (different streams, or different host threads
+ * without ordering) race on it and give wrong results; order them on one stream.
+ * No reference counterpart: the reference's kernel_ff always allocates its
+ * temporaries through torch.
+ */
+#define DSLPG_KERNEL_FF_STATIC_SCRATCH_BYTES ((int64_t)(16 * 1024 * 1024 + 64 * 1024))
+DSLPG_API int dslpg_kernel_ff_static(const void* x, const void* w1, const void* w3, const void* rms_w, void* out,
+                                     int64_t M, int64_t N, int64_t K, cudaStream_t stream);
 
 #ifdef __cplusplus
 }
