@@ -9,7 +9,9 @@
 //
 // Two kernels:
 //  * ff_prologue_kernel: one pass over x per row: a_norm and xs.
-//  * ff_gemm_kernel: persistent, one CTA per SM walking 128x128 output tiles,
+//  * ff_gemm2_kernel (M > 128): CTA pairs on 256x128 tiles with
+//    tcgen05.mma.cta_group::2 — described where it is defined;
+//  * ff_gemm_kernel (M <= 128): persistent, one CTA per SM walking 128x128 output tiles,
 //    warp-specialised:
 //      warp 0 (one lane)  TMA tensor loads of xs / w1 / w3 tiles (BK = 64,
 //                         128-byte swizzle) into a 4-stage shared-memory ring;
@@ -323,6 +325,270 @@ __global__ void __launch_bounds__(kFfThreads, 1)
   }
 }
 
+// ------------------------------------------------------- two-SM (CTA pair)
+// ff_gemm2_kernel: the same computation with 256x128 output tiles per CTA pair
+// (a cluster of 2 on neighbouring SMs) and ONE tcgen05.mma.cta_group::2 of
+// M = 256, N = 256 per K step, whose B operand is the w1 tile (128 rows, from
+// CTA 0's shared memory) stacked on the w3 tile (128 rows, from CTA 1's): the
+// accumulator's columns 0-127 are acc1 and 128-255 acc3. CTA r loads rows
+// [128r, 128r+128) of the xs tile and the w1 (r = 0) or w3 (r = 1) tile, so
+// each SM brings in 32 KiB per K-block of 64 (48 KiB with one CTA per tile)
+// and reads 64 bytes of operands per tensor cycle (A no longer read twice);
+// 6 stages fit in shared memory. Each CTA's TMEM holds its 128 rows of
+// acc1 | acc3 (two buffers, 512 columns).
+// Barriers: CTA 0's full[s] counts both CTAs' bytes (CTA 1's copies signal
+// it); empty[s] and tfull[b] are signalled in both CTAs by a multicast
+// tcgen05.commit; CTA 0's tempty[b] takes one arrival per epilogue warp of
+// both CTAs. TMA loads have no multicast.
+constexpr int kStages2 = 6;
+constexpr uint32_t kStage2Bytes = kTileA + kTileB;  // xs half-tile + this CTA's w1 or w3 tile
+constexpr size_t kFfSmem2 = 1024 + kStages2 * kStage2Bytes + 1024;
+// M = 256 (across the pair), N = 256 (w1 | w3), fp16 inputs, fp32 accumulator, K-major A and B.
+constexpr uint32_t kIdesc2 =
+    (1u << 4) | (static_cast<uint32_t>((2 * kBN) >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
+
+DSLPG_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+DSLPG_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Shared::cluster address of the same variable in CTA `rank` of the cluster.
+DSLPG_DEV uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+DSLPG_DEV void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// mbar_wait with cluster-scope acquire, for barriers the peer CTA signals.
+DSLPG_DEV bool mbar_wait_cl(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
+  const unsigned long long t0 = global_ns();
+  for (int n = 0;; ++n) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((n & 63) == 63 && global_ns() - t0 > limit_ns) return false;
+  }
+}
+
+DSLPG_DEV void umma2_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc2), "r"(accumulate));
+}
+
+// Arrive on barrier `bar` (same offset) in both CTAs of the pair once every
+// MMA issued so far by this thread has completed.
+DSLPG_DEV void umma2_commit_both(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+// Tensor load into this CTA's shared memory that signals `cluster_bar`, which
+// may be in either CTA of the pair.
+DSLPG_DEV void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFfThreads, 1)
+    ff_gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b1,
+                    const __grid_constant__ CUtensorMap map_b3, const FfArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t ring = (raw + 1023u) & ~1023u;  // same offset in both CTAs: the MMA reads both at it
+  const uint32_t bars = ring + kStages2 * kStage2Bytes;
+  const uint32_t full0 = bars, empty0 = bars + 8u * kStages2;
+  const uint32_t tfull0 = bars + 16u * kStages2, tempty0 = tfull0 + 16u, done_bar = tfull0 + 32u;
+  const int mt = static_cast<int>((a.M + 2 * kBM - 1) / (2 * kBM)), nt = static_cast<int>((a.N + kBN - 1) / kBN);
+  const int tiles = mt * nt;
+  const int kblocks = (a.K + kBK - 1) / kBK;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8u * b, 1);
+      mbar_init(tempty0 + 8u * b, 8);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == 1) {  // one warp of each CTA allocates for the pair
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producers
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = pair; t < tiles && !abort_flag; t += pairs) {
+        int tm, tn;
+        tile_coords(t, mt, nt, tm, tn);
+        const int arow = tm * 2 * kBM + static_cast<int>(rank) * kBM;
+        const CUtensorMap* map_b = rank == 0 ? &map_b1 : &map_b3;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % kStages2, ph = (it / kStages2) & 1u;
+          if (abort_flag) break;
+          if (it >= kStages2 && !mbar_wait_cl(empty0 + 8u * s, ph ^ 1u, kWaitLimitNs)) {
+            atomicAdd(&g_ff_timeouts, 1u);
+            abort_flag = 1;
+            break;
+          }
+          const uint32_t st = ring + s * kStage2Bytes;
+          const uint32_t fb = map_to_rank(full0 + 8u * s, 0);
+          if (rank == 0) mbar_arrive_expect_tx(full0 + 8u * s, 2 * kStage2Bytes);
+          tma_load_2d_pair(st, &map_a, kb * kBK, arow, fb);
+          tma_load_2d_pair(st + kTileA, map_b, kb * kBK, tn * kBN, fb);
+        }
+      }
+      // CTA 0's full barriers count the copies of both CTAs: it drains them
+      if (rank == 0)
+        for (uint32_t u = (it > kStages2 ? it - kStages2 : 0); u < it; ++u)
+          if (!mbar_wait_cl(full0 + 8u * (u % kStages2), (u / kStages2) & 1u, kWaitLimitNs))
+            atomicAdd(&g_ff_timeouts, 1u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA (CTA 0)
+    if (lane == 0 && rank == 0) {
+      uint32_t it = 0, j = 0;
+      for (int t = pair; t < tiles && !abort_flag; t += pairs, ++j) {
+        const uint32_t b = j & 1u;
+        if (j >= 2 && !mbar_wait_cl(tempty0 + 8u * b, ((j >> 1) & 1u) ^ 1u, kWaitLimitNs)) {
+          atomicAdd(&g_ff_timeouts, 1u);
+          abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc_base = tmem + b * 2u * kBN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const uint32_t s = it % kStages2;
+          if (abort_flag) break;
+          if (!mbar_wait_cl(full0 + 8u * s, (it / kStages2) & 1u, kWaitLimitNs)) {
+            atomicAdd(&g_ff_timeouts, 1u);
+            abort_flag = 1;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = ring + s * kStage2Bytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = smem_desc_sw128(st + 32u * k);
+            const uint64_t bd = smem_desc_sw128(st + kTileA + 32u * k);
+            umma2_f16(acc_base, ad, bd, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma2_commit_both(empty0 + 8u * s);
+        }
+        umma2_commit_both(tfull0 + 8u * b);
+      }
+      umma2_commit_both(done_bar);
+      if (!mbar_wait_cl(done_bar, 0u, kWaitLimitNs)) atomicAdd(&g_ff_timeouts, 1u);
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const uint32_t tempty_leader = map_to_rank(tempty0, 0);
+    uint32_t j = 0;
+    for (int t = pair; t < tiles; t += pairs, ++j) {
+      if (abort_flag) break;
+      const uint32_t b = j & 1u;
+      if (!mbar_wait_cl(tfull0 + 8u * b, (j >> 1) & 1u, kWaitLimitNs)) {
+        atomicAdd(&g_ff_timeouts, 1u);
+        abort_flag = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      int tm, tn;
+      tile_coords(t, mt, nt, tm, tn);
+      const int64_t m = static_cast<int64_t>(tm) * 2 * kBM + static_cast<int64_t>(rank) * kBM + 32 * q + lane;
+      const int64_t n0 = static_cast<int64_t>(tn) * kBN;
+      const bool row_ok = m < a.M;
+      const float an = row_ok ? a.a_norm[m] : 0.f;
+      const uint32_t lane_addr = tmem + b * 2u * kBN + (static_cast<uint32_t>(32 * q) << 16);
+      __half* orow = a.out + m * a.N;
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r1[32], r3[32];
+        tmem_ld32(lane_addr + 32u * c, r1);
+        tmem_ld32(lane_addr + kBN + 32u * c, r3);
+        if (c == kBN / 32 - 1) {  // both accumulators read: hand the buffer back to CTA 0's MMA thread
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(tempty_leader + 8u * b);
+        }
+        if (!row_ok) continue;
+        const int64_t nb = n0 + 32 * c;
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float v[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float g = __uint_as_float(r1[2 * i + h]) * an;
+            const float u = __uint_as_float(r3[2 * i + h]) * an;
+            const float sig = 1.0f / (1.0f + ex2(-g * kLog2e));
+            v[h] = (g * sig) * u;
+          }
+          packed[i] = pack2<__half>(v[0], v[1]);
+        }
+        if (nb + 32 <= a.N && (a.N % 8) == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            st_stream(orow + nb + 8 * i, Vec16{{packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]}});
+        } else {
+          for (int i = 0; i < 32; ++i) {
+            if (nb + i >= a.N) break;
+            const uint32_t w = packed[i >> 1];
+            orow[nb + i] = __ushort_as_half(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xffffu)));
+          }
+        }
+      }
+    }
+  }
+
+  // Neither CTA leaves (nor frees TMEM) while the pair's MMAs, copies or
+  // remote arrivals may still touch its memory.
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // ------------------------------------------------------------------- host
 namespace {
 
@@ -342,14 +608,14 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [rows, K] fp16 row-major, boxes of 128 rows x 64 columns, 128-byte swizzle,
+// [rows, K] fp16 row-major, boxes of box_rows rows x 64 columns, 128-byte swizzle,
 // zero fill out of bounds.
-bool make_map(CUtensorMap* map, const void* base, int64_t rows, int K) {
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int K, uint32_t box_rows = 128) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-  const cuuint32_t box[2] = {kBK, 128};
+  const cuuint32_t box[2] = {kBK, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -398,13 +664,34 @@ extern "C" int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, co
                                                 a_norm, M, static_cast<int>(K));
   if (cudaError_t e = cudaGetLastError()) return static_cast<int>(e);
 
+  FfArgs args{a_norm, static_cast<__half*>(out), M, N, static_cast<int>(K)};
+  const int path = kernel_path();
+  const bool use_pair = path == DSLPG_PATH_CLUSTER || (path != DSLPG_PATH_RESIDENT && M > kBM);
   CUtensorMap ma, mb1, mb3;
   if (!make_map(&ma, xs, M, static_cast<int>(K)) || !make_map(&mb1, w1, N, static_cast<int>(K)) ||
       !make_map(&mb3, w3, N, static_cast<int>(K)))
     return static_cast<int>(cudaErrorInvalidValue);
+  if (use_pair) {
+    const int64_t tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+    if (tiles > 0x3fffffff) return DSLPG_ERR_BAD_SHAPE;
+    const void* fn = reinterpret_cast<const void*>(&ff_gemm2_kernel);
+    if (cudaError_t e = allow_dynamic_smem(fn, kFfSmem2)) return static_cast<int>(e);
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kFfThreads);
+    cfg.dynamicSmemBytes = kFfSmem2;
+    cfg.stream = stream;
+    cfg.gridDim = dim3(2);
+    static int max_pairs = 0;  // co-resident CTA pairs (same device model for every device used)
+    if (max_pairs == 0) {
+      int n = 0;
+      if (cudaError_t e = cudaOccupancyMaxActiveClusters(&n, ff_gemm2_kernel, &cfg)) return static_cast<int>(e);
+      max_pairs = n > 0 ? n : 1;
+    }
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min<int64_t>(tiles, max_pairs)));
+    return static_cast<int>(cudaLaunchKernelEx(&cfg, ff_gemm2_kernel, ma, mb1, mb3, args));
+  }
   const void* fn = reinterpret_cast<const void*>(&ff_gemm_kernel);
   if (cudaError_t e = allow_dynamic_smem(fn, kFfSmem)) return static_cast<int>(e);
-  FfArgs args{a_norm, static_cast<__half*>(out), M, N, static_cast<int>(K)};
   const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
   if (tiles > 0x7fffffff) return DSLPG_ERR_BAD_SHAPE;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));  // one CTA per SM (TMEM: all 512 columns)

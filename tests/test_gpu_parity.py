@@ -408,16 +408,21 @@ def test_cross_entropy_few_long_rows(bs, smooth):
 
 
 # ------------------------------------------------ linear_activation.kernel_ff
+# path: "auto" (one CTA per tile for M <= 128, CTA pairs above), "resident"
+# (force one CTA per 128x128 tile), "cluster" (force CTA pairs on 256x128 tiles)
+@pytest.mark.parametrize("path", ["auto", "resident", "cluster"])
 @pytest.mark.parametrize("b,s,d,n", [(1, 128, 64, 128), (1, 128, 128, 256), (2, 100, 512, 200), (1, 256, 1024, 512),
-                                     (1, 300, 2048, 640), (3, 7, 72, 40)])
-def test_kernel_ff(b, s, d, n):
+                                     (1, 300, 2048, 640), (3, 7, 72, 40), (1, 1000, 320, 1000), (4, 700, 256, 2176)])
+def test_kernel_ff(b, s, d, n, path):
     g = gen(d + n)
     x = randn((b, s, d), torch.float16, g)
     w1 = randn((n, d), torch.float16, g, std=d ** -0.5)
     w3 = randn((n, d), torch.float16, g, std=d ** -0.5)
     rw = randn((d,), torch.float16, g, mean=1.0, std=0.1)
-    out = B.kernel_ff(x.cuda(), w1.cuda(), w3.cuda(), rw.cuda())
+    with _lib.kernel_path(path):
+        out = B.kernel_ff(x.cuda(), w1.cuda(), w3.cuda(), rw.cuda())
     ref = oracle.kernel_ff(x, w1, w3, rw)
+    assert _lib.take_wait_timeouts() == 0
     assert out.shape == ref.shape and out.dtype == torch.float16
     ok, msg = parity.compare(out, ref, torch.float16, abs_slack=parity.GEMM_SLACK * ref.float().abs().max().item())
     assert ok, msg
