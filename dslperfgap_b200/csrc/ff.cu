@@ -340,7 +340,10 @@ __global__ void __launch_bounds__(kFfThreads, 1)
 // it); empty[s] and tfull[b] are signalled in both CTAs by a multicast
 // tcgen05.commit; CTA 0's tempty[b] takes one arrival per epilogue warp of
 // both CTAs. TMA loads have no multicast.
-constexpr int kStages2 = 6;
+#ifndef DSLPG_FF_STAGES
+#define DSLPG_FF_STAGES 6
+#endif
+constexpr int kStages2 = DSLPG_FF_STAGES;
 constexpr uint32_t kStage2Bytes = kTileA + kTileB;  // xs half-tile + this CTA's w1 or w3 tile
 constexpr size_t kFfSmem2 = 1024 + kStages2 * kStage2Bytes + 1024;
 // M = 256 (across the pair), N = 256 (w1 | w3), fp16 inputs, fp32 accumulator, K-major A and B.
