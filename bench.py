@@ -368,8 +368,21 @@ def torch_baseline(wl):
 
 
 def eager_reference_expression(wl):
-    """The reference's pytorch_impl computation written as eager torch (RMSNorm only:
-    pytorch_impl.rms_norm is 5 kernels, the other pytorch_impls are one torch op)."""
+    """The reference's pytorch_impl computation written as eager torch, for the ops
+    whose pytorch_impl is more than one torch op: rms_norm (5 kernels) and
+    linear_activation.kernel_ff (fp32 matmuls, ViperBench/linear_activation/pytorch_impl.py:5-54)."""
+    if wl.config.op == "linear_activation":
+        x, w1, w3, rw = wl.args
+        K = wl.config.K
+
+        def ff():
+            xf = x.reshape(-1, K)
+            an = torch.rsqrt((xf.float() ** 2).sum(-1) / K + 1e-6)
+            xs = (xf * rw.unsqueeze(0)).float()
+            a1 = (xs @ w1.float().T) * an.unsqueeze(1)
+            a2 = (xs @ w3.float().T) * an.unsqueeze(1)
+            return ((a1 * torch.sigmoid(a1)) * a2).half()
+        return ff
     if wl.config.op != "rms_norm":
         return None
     x, w, eps = wl.args[0], wl.args[2], wl.kwargs.get("eps", 1e-5)
@@ -427,6 +440,15 @@ def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler
             t_e = timer.max_over_ranks(sum(te)) / steps
             res["torch_eager_pytorch_impl_ms"] = round(t_e, 5)
             res["e_lib_vs_pytorch_impl_pct"] = round(100.0 * t_e / ms_step, 1)
+        if cfg.op == "linear_activation":
+            # the GEMM alone through cuBLAS: xs @ [w1; w3]^T, fp16 (no norm, no gate)
+            xs = (wl.args[0].reshape(-1, cfg.K) * wl.args[3]).contiguous()
+            w13 = torch.cat([wl.args[1], wl.args[2]], 0)
+            tg = timer.time_steps(lambda: xs @ w13.t(), steps, warmup)
+            t_g = timer.max_over_ranks(sum(tg)) / steps
+            res["cublas_gemm_only_ms"] = round(t_g, 5)
+            res["cublas_gemm_only_tflops"] = round(flops / (t_g * 1e-3) / 1e12, 1)
+            del xs, w13
     del launch, wl
     torch.cuda.empty_cache()
     return res
