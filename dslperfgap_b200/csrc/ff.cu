@@ -8,7 +8,7 @@
 // (ViperBench/linear_activation/pytorch_impl.py:5-54.)
 //
 // Two kernels:
-//  * ff_prologue_kernel: one pass over x per row: a_norm and xs.
+//  * ff_prologue_kernel: one pass over x per row (a warp per row): a_norm and xs.
 //  * ff_gemm2_kernel (M > 128): CTA pairs on 256x128 tiles with
 //    tcgen05.mma.cta_group::2 — described where it is defined;
 //  * ff_gemm_kernel (M <= 128): persistent, one CTA per SM walking 128x128 output tiles,
@@ -48,35 +48,44 @@ constexpr uint32_t kFfThreads = 192;
 constexpr size_t kFfSmem = 1024 + kStages * kStageBytes + 1024;  // alignment + ring + barriers
 
 // ---------------------------------------------------------------- prologue
-// One CTA (256 threads) per row group, 16-byte vectors; K % 8 == 0.
+// One warp per row (8 rows per CTA of 256 threads, rows strided over a
+// persistent grid), 16-byte vectors with 4 in flight per lane; K % 8 == 0.
 __global__ void __launch_bounds__(256) ff_prologue_kernel(const __half* __restrict__ x, const __half* __restrict__ w,
                                                           __half* __restrict__ xs, float* __restrict__ a_norm,
                                                           int64_t M, int K) {
-  __shared__ float red[32];
-  const int nvec = K / 8;
-  for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
+  constexpr int U = 4;
+  const int nvec = K / 8, lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t m = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps) {
     const __half* xr = x + m * K;
     __half* yr = xs + m * K;
     float ss = 0.f;
-    for (int j = threadIdx.x; j < nvec; j += blockDim.x) {
-      const Vec16 v = ld_stream(xr + static_cast<int64_t>(j) * 8);
-      const Vec16 wv = ld_keep(w + static_cast<int64_t>(j) * 8);
-      Vec16 o;
+    for (int j0 = lane; j0 < nvec; j0 += 32 * U) {
+      Vec16 v[U];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __half2 a = *reinterpret_cast<const __half2*>(&v.w[i]);
-        const __half2 b = *reinterpret_cast<const __half2*>(&wv.w[i]);
-        const float2 af = __half22float2(a);
-        ss = fmaf(af.x, af.x, ss);
-        ss = fmaf(af.y, af.y, ss);
-        const __half2 p = __hmul2(a, b);  // x * rms_w in fp16, as the reference
-        o.w[i] = *reinterpret_cast<const uint32_t*>(&p);
+      for (int u = 0; u < U; ++u)
+        if (j0 + 32 * u < nvec) v[u] = ld_stream(xr + static_cast<int64_t>(j0 + 32 * u) * 8);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + 32 * u;
+        if (j >= nvec) break;
+        const Vec16 wv = ld_keep(w + static_cast<int64_t>(j) * 8);
+        Vec16 o;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __half2 a = *reinterpret_cast<const __half2*>(&v[u].w[i]);
+          const __half2 b = *reinterpret_cast<const __half2*>(&wv.w[i]);
+          const float2 af = __half22float2(a);
+          ss = fmaf(af.x, af.x, ss);
+          ss = fmaf(af.y, af.y, ss);
+          const __half2 p = __hmul2(a, b);  // x * rms_w in fp16, as the reference
+          o.w[i] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        st_stream(yr + static_cast<int64_t>(j) * 8, o);
       }
-      st_stream(yr + static_cast<int64_t>(j) * 8, o);
     }
-    ss = group_reduce<SumOp>(ss, red, blockDim.x >> 5, 0);
-    if (threadIdx.x == 0) a_norm[m] = rsqrtf(ss / static_cast<float>(K) + 1e-6f);
-    __syncthreads();
+    ss = warp_reduce<SumOp>(ss);
+    if (lane == 0) a_norm[m] = rsqrtf(ss / static_cast<float>(K) + 1e-6f);
   }
 }
 
@@ -128,6 +137,32 @@ DSLPG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : DSLPG_R32(r)
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+DSLPG_DEV float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// out = silu(a_norm * acc1) * (a_norm * acc3) for 32 columns of one row, in
+// f32x2 pairs: sigmoid(g) = 1 / (1 + 2^(-g log2 e)) with the SFU's ex2 and
+// reciprocal (a few fp32 ulps, far below the fp16 output's rounding), then
+// rounded to fp16 pairs.
+DSLPG_DEV void gate_pack(const uint32_t (&r1)[32], const uint32_t (&r3)[32], float an, uint32_t (&packed)[16]) {
+  const f32x2 an2 = pk2(an, an), nl2 = pk2(-kLog2e, -kLog2e), one2 = pk2(1.0f, 1.0f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const f32x2 g = mul2(pk2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1])), an2);
+    const f32x2 u = mul2(pk2(__uint_as_float(r3[2 * i]), __uint_as_float(r3[2 * i + 1])), an2);
+    float t0, t1;
+    upk2(mul2(g, nl2), t0, t1);
+    float d0, d1;
+    upk2(add2(pk2(ex2(t0), ex2(t1)), one2), d0, d1);
+    float v0, v1;
+    upk2(mul2(mul2(g, pk2(rcp_approx(d0), rcp_approx(d1))), u), v0, v1);
+    packed[i] = pack2<__half>(v0, v1);
+  }
 }
 
 struct FfArgs {
@@ -290,18 +325,7 @@ __global__ void __launch_bounds__(kFfThreads, 1)
         if (!row_ok) continue;
         const int64_t nb = n0 + 32 * c;
         uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float g = __uint_as_float(r1[2 * i + h]) * an;
-            const float u = __uint_as_float(r3[2 * i + h]) * an;
-            const float sig = 1.0f / (1.0f + ex2(-g * kLog2e));
-            v[h] = (g * sig) * u;
-          }
-          packed[i] = pack2<__half>(v[0], v[1]);
-        }
+        gate_pack(r1, r3, an, packed);
         if (nb + 32 <= a.N && (a.N % 8) == 0) {
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -551,21 +575,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFfThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(tempty_leader + 8u * b);
         }
+        #ifdef DSLPG_FF_DIAG_NO_EPILOGUE  // diagnostic builds only: time the main loop without the epilogue's math and stores
+        continue;
+#endif
         if (!row_ok) continue;
         const int64_t nb = n0 + 32 * c;
         uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float g = __uint_as_float(r1[2 * i + h]) * an;
-            const float u = __uint_as_float(r3[2 * i + h]) * an;
-            const float sig = 1.0f / (1.0f + ex2(-g * kLog2e));
-            v[h] = (g * sig) * u;
-          }
-          packed[i] = pack2<__half>(v[0], v[1]);
-        }
+        gate_pack(r1, r3, an, packed);
         if (nb + 32 <= a.N && (a.N % 8) == 0) {
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -662,7 +678,7 @@ extern "C" int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, co
   __half* xs = static_cast<__half*>(workspace);
   float* a_norm = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((M * K * 2 + 255) / 256) * 256);
 
-  const int pgrid = persistent_grid(reinterpret_cast<const void*>(&ff_prologue_kernel), 256, 0, M);
+  const int pgrid = persistent_grid(reinterpret_cast<const void*>(&ff_prologue_kernel), 256, 0, (M + 7) / 8);
   ff_prologue_kernel<<<pgrid, 256, 0, stream>>>(static_cast<const __half*>(x), static_cast<const __half*>(rms_w), xs,
                                                 a_norm, M, static_cast<int>(K));
   if (cudaError_t e = cudaGetLastError()) return static_cast<int>(e);
