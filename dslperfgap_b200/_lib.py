@@ -47,6 +47,8 @@ SIGNATURES = {
     "dslpg_argmax": [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "dslpg_kernel_ff_workspace_bytes": [_c_i64, _c_i64, _vp],
     "dslpg_kernel_ff": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_i64, _vp],
+    "dslpg_rms_norm_fwd_host_workspace_bytes": [_c_i64, _c_i64, _c_int, _vp],
+    "dslpg_rms_norm_fwd_host": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_f32, _vp, _c_i64, _vp],
     "dslpg_kernel_ff_static": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp],
     "dslpg_version": [],
     "dslpg_set_kernel_path": [_c_int],

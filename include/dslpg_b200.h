@@ -197,6 +197,27 @@ DSLPG_API int dslpg_argmax(const void* x, int64_t* indices, int64_t M, int64_t N
                            cudaStream_t stream);
 
 /*
+ * dslpg_rms_norm_fwd on HOST buffers: x_host [M, N] (x_dtype) in, y_host
+ * [M, N] out; weight is a device pointer. The rows stream through the GPU in
+ * chunks of about 16 MiB, the upload of one chunk, the kernel on the previous
+ * one and the download of the one before overlapping (two copy streams of
+ * this library plus `stream`; one cudaMemcpyAsync per chunk and direction).
+ * With pinned host memory the copies run asynchronously in both directions at
+ * once; pageable memory works but the copies do not overlap. `workspace`
+ * (device, 256-byte aligned) holds the chunk buffers: at least
+ * dslpg_rms_norm_fwd_host_workspace_bytes(M, N, x_dtype) bytes. The call
+ * returns once the work is enqueued; everything is ordered on `stream`, so
+ * synchronise it before reading y_host. Calls on one device are serialised by
+ * a lock while they enqueue. Same result as dslpg_rms_norm_fwd row by row.
+ * Serves the reference's rms_norm (ViperBench/rms_norm/pytorch_impl.py:3-10)
+ * for inputs that live in host memory.
+ */
+DSLPG_API int dslpg_rms_norm_fwd_host_workspace_bytes(int64_t M, int64_t N, int x_dtype, int64_t* bytes);
+DSLPG_API int dslpg_rms_norm_fwd_host(const void* x_host, const void* weight, void* y_host, int64_t M, int64_t N,
+                                      int x_dtype, int w_dtype, float eps, void* workspace, int64_t workspace_bytes,
+                                      cudaStream_t stream);
+
+/*
  * Llama feed-forward with the RMSNorm fused around a tensor-core dual GEMM:
  *   a_norm[m] = rsqrt(sum_k x[m,k]^2 / K + 1e-6);  xs = x * rms_w (fp16);
  *   out[m,n] = silu(a_norm[m] * (xs @ w1^T)[m,n]) * (a_norm[m] * (xs @ w3^T)[m,n])   (fp16)
