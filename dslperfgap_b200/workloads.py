@@ -1,5 +1,5 @@
-"""Synthetic benchmark workloads: the five configurations the backend is
-measured on, as seeded generators.
+"""Synthetic benchmark workloads: the configurations the backend is measured
+on, as seeded generators.
 
 The reference measures on internal synthetic shapes only (no dataset), so
 these generators are the whole workload. Values follow the stated
@@ -17,7 +17,9 @@ each output written once:
   cross_entropy (one block per row)              M * N * elem_size + 8 * M + 3 * 4 * M
   cross_entropy_bwd                              2 * M * N * elem_size + 8 * M + 4 * M + 4 * M
   mean_reduction / max_reduction / argmax        M * N * elem_size + the M outputs
-(the [N] weight and bias vectors, read once per GPU, are not counted).
+  linear_activation (kernel_ff)                  (M*K + 2*N*K + K + M*N) * 2; its roofline is
+                                                 tensor-bound: 4 * M * N * K flops
+(the [N] weight and bias vectors of the row ops, read once per GPU, are not counted).
 """
 from __future__ import annotations
 
@@ -75,13 +77,13 @@ CONFIGS = {
                "max (values, indices) over dim 1, fp16 x[8192,32768]~N(0,1) (benchmark.py:278-280)", {"dim": 1}),
         Config("argmax_fp16", "argmax", "argmax", 8192, 32768, torch.float16,
                "argmax over dim 1, fp16 x[8192,32768]~N(0,1) (benchmark.py:97-99)", {"dim": 1}),
+        Config("layer_norm_bf16_sharded", "layer_norm", "layer_norm", 131072, 8192, torch.bfloat16,
+               "row-sharded LayerNorm bf16 x[131072,8192]~N(0,1), w~N(1,0.1), b~N(0,0.1), eps=1e-5, "
+               "row blocks over 1/2/4/8 GPUs", {"eps": 1e-5}),
         Config("linear_activation_fp16", "linear_activation", "kernel_ff", 2048, 16384, torch.float16,
                "Llama FFN kernel_ff fp16: x[1,2048,4096], w1/w3[16384,4096], rms_w[4096] ~N(0,1) "
                "(the reference's large shape, benchmark.py:223-228); RMSNorm + dual GEMM + SiLU gate",
                {}, K=4096),
-        Config("layer_norm_bf16_sharded", "layer_norm", "layer_norm", 131072, 8192, torch.bfloat16,
-               "row-sharded LayerNorm bf16 x[131072,8192]~N(0,1), w~N(1,0.1), b~N(0,0.1), eps=1e-5, "
-               "row blocks over 1/2/4/8 GPUs", {"eps": 1e-5}),
     ]
 }
 NAMES = list(CONFIGS)
