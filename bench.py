@@ -503,6 +503,16 @@ PUBLISHED = {
     "max_reduction x:(8192,32768) dim=1 fp16": ("GH200", 95, (0.2779, 0.2288, 0.3319)),
     "mean_reduction x:(8192,32768) dim=1 fp32": ("GH200", 101, (0.3029, 0.649, 0.3146)),
     "linear_activation x:(1,2048,4096) w1/w3:(16384,4096) fp16": ("A100-PCIE-40GB", 65, (33.0058, 45.6209, 9.4071)),
+    "layer_norm x:(512,1024) bf16": ("GH200", 50, (0.0184, 0.0656, 0.5406)),
+    "rms_norm x:(512,1024) fp16": ("GH200", 116, (0.104, 0.0493, 0.4824)),
+    "softmax x:(512,1024) fp16": ("GH200", 122, (0.0164, 0.0359, 0.0351)),
+    "log_softmax x:(512,1024) fp16": ("GH200", 68, (0.0177, 0.0546, 0.0488)),
+    "logsumexp x:(512,1024) fp32": ("GH200", 74, (0.0844, 0.1599, 0.0604)),
+    "cross_entropy logits:(256,1024) fp32 BLOCK 256": ("GH200", 32, (0.5406, 0.0782, 0.1269)),
+    "argmax x:(1024,1024) dim=1 fp16": ("GH200", 8, (0.022, 0.0698, 0.0941)),
+    "max_reduction x:(1024,1024) dim=1 fp16": ("GH200", 92, (0.0236, 0.0544, 0.0934)),
+    "mean_reduction x:(1024,1024) dim=1 fp32": ("GH200", 98, (0.0177, 0.0458, 0.0481)),
+    "linear_activation x:(1,256,1024) w1/w3:(4096,1024) fp16": ("GH200", 62, (0.3617, 0.1205, 0.3082)),
 }
 
 
@@ -535,51 +545,61 @@ def reference_shapes(dev):
         hw, line, (pt, tr, tl) = PUBLISHED[name]
         ms = reference_protocol_ms(ours)
         lib_ms = reference_protocol_ms(lib)
+        src = "GH200-480GB" if hw == "GH200" else hw
         out[name] = {"ms": round(ms, 4), "torch_op": lib_name, "torch_ms": round(lib_ms, 4),
                      "e_lib_pct": round(100 * lib_ms / ms, 1),
                      "published_ms": {"hardware": hw, "pytorch": pt, "triton": tr, "tilelang": tl,
-                                      "source": f"ViperBench/results/profile.{'GH200-480GB' if hw == 'GH200' else hw}.csv:{line}"}}
+                                      "source": f"ViperBench/results/profile.{src}.csv:{line}"}}
 
-    x = rn(8192, 8192, dtype=torch.bfloat16)
-    w, b = rn(8192, dtype=torch.bfloat16), rn(8192, dtype=torch.bfloat16)
-    case("layer_norm x:(8192,8192) bf16", lambda: B.layer_norm(x, w, b), lambda: F.layer_norm(x, (8192,), w, b, 1e-5),
-         "F.layer_norm")
-    x = rn(8192, 8192, dtype=torch.float16)
-    w = rn(8192, dtype=torch.float16)
-    case("rms_norm x:(8192,8192) fp16", lambda: B.rms_norm(x, (8192,), w), lambda: F.rms_norm(x, (8192,), w, 1e-5),
-         "F.rms_norm")
-    x = rn(4096, 32768, dtype=torch.float16)
-    case("softmax x:(4096,32768) fp16", lambda: B.softmax(x), lambda: F.softmax(x, -1), "F.softmax")
-    case("log_softmax x:(4096,32768) fp16", lambda: B.log_softmax(x), lambda: F.log_softmax(x, -1), "F.log_softmax")
-    x = rn(8192, 16384, dtype=torch.float32)
-    case("logsumexp x:(8192,16384) fp32", lambda: B.logsumexp(x), lambda: torch.logsumexp(x, -1), "torch.logsumexp")
+    for m, n in ((8192, 8192), (512, 1024)):
+        x = rn(m, n, dtype=torch.bfloat16)
+        w, b = rn(n, dtype=torch.bfloat16), rn(n, dtype=torch.bfloat16)
+        case(f"layer_norm x:({m},{n}) bf16", lambda: B.layer_norm(x, w, b),
+             lambda: F.layer_norm(x, (n,), w, b, 1e-5), "F.layer_norm")
+        x = rn(m, n, dtype=torch.float16)
+        w = rn(n, dtype=torch.float16)
+        case(f"rms_norm x:({m},{n}) fp16", lambda: B.rms_norm(x, (n,), w), lambda: F.rms_norm(x, (n,), w, 1e-5),
+             "F.rms_norm")
+    for m, n in ((4096, 32768), (512, 1024)):
+        x = rn(m, n, dtype=torch.float16)
+        case(f"softmax x:({m},{n}) fp16", lambda: B.softmax(x), lambda: F.softmax(x, -1), "F.softmax")
+        case(f"log_softmax x:({m},{n}) fp16", lambda: B.log_softmax(x), lambda: F.log_softmax(x, -1),
+             "F.log_softmax")
+    for m, n in ((8192, 16384), (512, 1024)):
+        x = rn(m, n, dtype=torch.float32)
+        case(f"logsumexp x:({m},{n}) fp32", lambda: B.logsumexp(x), lambda: torch.logsumexp(x, -1),
+             "torch.logsumexp")
     del x
-    lg = rn(4096, 32768, dtype=torch.float32)
-    lb = torch.randint(0, 32768, (4096,), generator=g, device=dev, dtype=torch.int64)
-    ce_args = (0.0, 1.0, 0.0, -100, 32768, 0, 1024, False, False)
-    case("cross_entropy logits:(4096,32768) fp32 BLOCK 1024", lambda: B.cross_entropy_fwd(lg, lb, *ce_args),
-         lambda: F.cross_entropy(lg, lb, ignore_index=-100, reduction="none"), "F.cross_entropy(reduction='none')")
-    del lg
-    x = rn(8192, 32768, dtype=torch.float16)
-    case("argmax x:(8192,32768) dim=1 fp16", lambda: B.argmax(x, 1), lambda: torch.argmax(x, 1), "torch.argmax")
-    case("max_reduction x:(8192,32768) dim=1 fp16", lambda: B.max_reduction(x, 1), lambda: torch.max(x, 1),
-         "torch.max(dim)")
-    x = rn(8192, 32768, dtype=torch.float32)
-    case("mean_reduction x:(8192,32768) dim=1 fp32", lambda: B.mean_reduction(x, 1), lambda: torch.mean(x, 1),
-         "torch.mean")
-    del x
-    x = rn(1, 2048, 4096, dtype=torch.float16)
-    w1, w3 = rn(16384, 4096, dtype=torch.float16), rn(16384, 4096, dtype=torch.float16)
-    rw = rn(4096, dtype=torch.float16)
+    for m, n, bs in ((4096, 32768, 1024), (256, 1024, 256)):
+        lg = rn(m, n, dtype=torch.float32)
+        lb = torch.randint(0, n, (m,), generator=g, device=dev, dtype=torch.int64)
+        ce_args = (0.0, 1.0, 0.0, -100, n, 0, bs, False, False)
+        case(f"cross_entropy logits:({m},{n}) fp32 BLOCK {bs}", lambda: B.cross_entropy_fwd(lg, lb, *ce_args),
+             lambda: F.cross_entropy(lg, lb, ignore_index=-100, reduction="none"),
+             "F.cross_entropy(reduction='none')")
+        del lg
+    for m, n in ((8192, 32768), (1024, 1024)):
+        x = rn(m, n, dtype=torch.float16)
+        case(f"argmax x:({m},{n}) dim=1 fp16", lambda: B.argmax(x, 1), lambda: torch.argmax(x, 1), "torch.argmax")
+        case(f"max_reduction x:({m},{n}) dim=1 fp16", lambda: B.max_reduction(x, 1), lambda: torch.max(x, 1),
+             "torch.max(dim)")
+        x = rn(m, n, dtype=torch.float32)
+        case(f"mean_reduction x:({m},{n}) dim=1 fp32", lambda: B.mean_reduction(x, 1), lambda: torch.mean(x, 1),
+             "torch.mean")
+        del x
+    for s_, k, nn in ((2048, 4096, 16384), (256, 1024, 4096)):
+        x = rn(1, s_, k, dtype=torch.float16)
+        w1, w3 = rn(nn, k, dtype=torch.float16), rn(nn, k, dtype=torch.float16)
+        rw = rn(k, dtype=torch.float16)
 
-    def ff_torch():  # the same computation with cuBLAS fp16 GEMMs and an eager epilogue
-        xf = x.reshape(-1, 4096)
-        an = torch.rsqrt(xf.float().pow(2).mean(-1, keepdim=True) + 1e-6)
-        xs = xf * rw
-        return (F.silu((xs @ w1.t()).float() * an) * ((xs @ w3.t()).float() * an)).half()
-    case("linear_activation x:(1,2048,4096) w1/w3:(16384,4096) fp16", lambda: B.kernel_ff(x, w1, w3, rw), ff_torch,
-         "cuBLAS fp16 GEMMs + eager epilogue")
-    del x, w1, w3
+        def ff_torch():  # the same computation with cuBLAS fp16 GEMMs and an eager epilogue
+            xf = x.reshape(-1, k)
+            an = torch.rsqrt(xf.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+            xs = xf * rw
+            return (F.silu((xs @ w1.t()).float() * an) * ((xs @ w3.t()).float() * an)).half()
+        case(f"linear_activation x:(1,{s_},{k}) w1/w3:({nn},{k}) fp16", lambda: B.kernel_ff(x, w1, w3, rw), ff_torch,
+             "cuBLAS fp16 GEMMs + eager epilogue")
+        del x, w1, w3
     torch.cuda.empty_cache()
     return {"protocol": "ViperBench/benchmark.py:26-58 (perf_counter + synchronize per call, median of 100 after 10)",
             "data": "torch.randn on the device, seed 0 (the reference's shapes and distributions)", "cases": out}

@@ -120,6 +120,53 @@ def stream_handle(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+_get_device = torch._C._cuda_getDevice
+_raw_stream = torch._C._cuda_getCurrentRawStream
+
+
+_fast = None  # the _dslpg_fast extension module, or False when not used
+
+
+def fast_module():
+    """The METH_FASTCALL binding of the per-call entry points (built next to the
+    library), or None. Not used when DSLPG_LIB selects another library build:
+    the extension is linked to the default one."""
+    global _fast
+    if _fast is None:
+        load()  # the library itself first, from LIB_PATH
+        mod = False
+        if not os.environ.get("DSLPG_LIB"):
+            import importlib.machinery
+            import importlib.util
+            from .build import FAST_PATH
+            if FAST_PATH.exists():
+                loader = importlib.machinery.ExtensionFileLoader("_dslpg_fast", str(FAST_PATH))
+                spec = importlib.util.spec_from_file_location("_dslpg_fast", str(FAST_PATH), loader=loader)
+                mod = importlib.util.module_from_spec(spec)
+                loader.exec_module(mod)
+        _fast = mod
+    return _fast or None
+
+
+def launch(dev: torch.device, name: str, *args) -> None:
+    """Call entry point `name`(*args, stream) on `dev` with that device's current
+    stream appended; raise RuntimeError on a non-zero return. The current device
+    is switched (and restored) only when it is not `dev` already. Goes through
+    the _dslpg_fast extension when it has the entry point, else ctypes."""
+    fast = _fast if _fast is not None else fast_module()
+    fn = getattr(fast, name, None) if fast else None
+    if fn is None:
+        fn = getattr(_lib if _lib is not None else load(), name)
+    idx = dev.index if dev.index is not None else _get_device()
+    if _get_device() == idx:
+        rc = fn(*args, _raw_stream(idx))
+    else:
+        with torch.cuda.device(idx):
+            rc = fn(*args, _raw_stream(idx))
+    if rc != 0:
+        check(rc, name)
+
+
 class kernel_path:
     """Context manager forcing one kernel shape ("auto", "resident", "tma",
     "stream") for the calls made inside it (process-wide; for tests and

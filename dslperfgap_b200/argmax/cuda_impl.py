@@ -26,7 +26,5 @@ def argmax(input_tensor, dim, keepdim=False):
     indices = torch.empty(oshape, dtype=torch.int64, device=x.device)
     if indices.numel() == 0:
         return indices
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_argmax(x.data_ptr(), indices.data_ptr(), m, n, k, code, _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_argmax")
+    _lib.launch(dev, "dslpg_argmax", x.data_ptr(), indices.data_ptr(), m, n, k, code)
     return indices

@@ -2,7 +2,10 @@
 
 The library is compiled in-tree with nvcc for sm_100a only:
 each ``csrc/*.cu`` becomes an object (in parallel), and the objects are linked
-into one shared library against the CUDA runtime. Re-running is cheap: an
+into one shared library against the CUDA runtime. ``csrc/pyfast.c`` then
+becomes the CPython extension ``lib/_dslpg_fast*.so`` (gcc, linked to the
+library through an ``$ORIGIN`` run path): the low-overhead binding of the
+per-call entry points. Re-running is cheap: an
 object is rebuilt only when a source or header under ``csrc/`` or ``include/``
 is newer than it.
 
@@ -16,6 +19,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
@@ -26,6 +30,8 @@ BUILD_DIR = PKG_DIR / "_build"
 LIB_DIR = PKG_DIR / "lib"
 LIB_NAME = "libdslpg_b200.so"
 LIB_PATH = LIB_DIR / LIB_NAME
+FAST_PATH = LIB_DIR / ("_dslpg_fast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+CUDA_INCLUDE = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -91,12 +97,32 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False, 
     relink = bool(todo) or not lib_path.exists() or any(o.stat().st_mtime > lib_path.stat().st_mtime for o in objs)
     if relink:
         tmp = lib_path.parent / (lib_path.name + ".tmp")
-        cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
+        cmd = [nvcc_path(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart",
+               "-Xlinker", f"-soname={LIB_NAME}"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
         os.replace(tmp, lib_path)
+    if out is None:
+        build_fast(force=relink or force)
     return lib_path
+
+
+def build_fast(force: bool = False) -> Path:
+    """Compile csrc/pyfast.c into the CPython extension next to the library."""
+    src = CSRC / "pyfast.c"
+    if not force and FAST_PATH.exists() and FAST_PATH.stat().st_mtime >= max(
+            src.stat().st_mtime, LIB_PATH.stat().st_mtime, _newest_header_mtime()):
+        return FAST_PATH
+    tmp = FAST_PATH.parent / (FAST_PATH.name + ".tmp")
+    cmd = [os.environ.get("CC", "gcc"), "-O2", "-shared", "-fPIC", "-fvisibility=hidden",
+           "-I", sysconfig.get_paths()["include"], "-I", str(INCLUDE), "-I", str(CUDA_INCLUDE),
+           str(src), "-o", str(tmp), "-L", str(LIB_DIR), "-ldslpg_b200", "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"building {FAST_PATH.name} failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, FAST_PATH)
+    return FAST_PATH
 
 
 def main(argv=None) -> int:

@@ -47,14 +47,13 @@ def cross_entropy_fwd(
     z_loss = torch.empty((n_rows, n_cols), dtype=torch.float32, device=logits.device)
     if n_rows == 0 or n_cols == 0:
         return loss, lse, z_loss
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_cross_entropy_fwd(
-            logits.data_ptr(), labels.data_ptr(), loss.data_ptr(), lse.data_ptr(), z_loss.data_ptr(),
-            n_rows, n_cols, logits.stride(0), lcode, _lib.LABEL_CODES[labels.dtype],
-            float(smoothing), float(logit_scale), float(lse_square_scale), int(ignored_index),
-            float(total_classes), int(class_start_idx), int(BLOCK_SIZE),
-            1 if HAS_SMOOTHING else 0, 1 if SPLIT else 0, _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_cross_entropy_fwd")
+    _lib.launch(
+        dev, "dslpg_cross_entropy_fwd",
+        logits.data_ptr(), labels.data_ptr(), loss.data_ptr(), lse.data_ptr(), z_loss.data_ptr(),
+        n_rows, n_cols, logits.stride(0), lcode, _lib.LABEL_CODES[labels.dtype],
+        float(smoothing), float(logit_scale), float(lse_square_scale), int(ignored_index),
+        float(total_classes), int(class_start_idx), int(BLOCK_SIZE),
+        1 if HAS_SMOOTHING else 0, 1 if SPLIT else 0)
     return loss, lse, z_loss
 
 
@@ -88,11 +87,10 @@ def cross_entropy_bwd(
     dlogits = torch.empty((n_rows, n_cols), dtype=logits.dtype, device=logits.device)
     if n_rows == 0 or n_cols == 0:
         return dlogits
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_cross_entropy_bwd(
-            dloss.data_ptr(), dcode, dloss.stride(0), logits.data_ptr(), lse_flat.data_ptr(), labels.data_ptr(),
-            dlogits.data_ptr(), n_rows, n_cols, logits.stride(0), n_cols, lcode, _lib.LABEL_CODES[labels.dtype],
-            float(smoothing), float(logit_scale), float(lse_square_scale), int(ignored_index),
-            float(total_classes), int(class_start_idx), 1 if HAS_SMOOTHING else 0, _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_cross_entropy_bwd")
+    _lib.launch(
+        dev, "dslpg_cross_entropy_bwd",
+        dloss.data_ptr(), dcode, dloss.stride(0), logits.data_ptr(), lse_flat.data_ptr(), labels.data_ptr(),
+        dlogits.data_ptr(), n_rows, n_cols, logits.stride(0), n_cols, lcode, _lib.LABEL_CODES[labels.dtype],
+        float(smoothing), float(logit_scale), float(lse_square_scale), int(ignored_index),
+        float(total_classes), int(class_start_idx), 1 if HAS_SMOOTHING else 0)
     return dlogits

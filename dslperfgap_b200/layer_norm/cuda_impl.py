@@ -34,9 +34,6 @@ def layer_norm(x, weight, bias, eps=1e-5):
     y = torch.empty_like(x)
     if x.numel() == 0:
         return y
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_layer_norm_fwd(
-            x.data_ptr(), w.data_ptr(), b.data_ptr() if b is not None else None, y.data_ptr(),
-            m, n, xc, wc, float(eps), _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_layer_norm_fwd")
+    _lib.launch(dev, "dslpg_layer_norm_fwd", x.data_ptr(), w.data_ptr(), b.data_ptr() if b is not None else None, y.data_ptr(),
+            m, n, xc, wc, float(eps))
     return y

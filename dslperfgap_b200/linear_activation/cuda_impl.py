@@ -40,8 +40,6 @@ def kernel_ff(x, w1, w3, rms_w):
     need = ctypes.c_int64(0)
     _lib.check(lib.dslpg_kernel_ff_workspace_bytes(m, dim, ctypes.byref(need)), "dslpg_kernel_ff_workspace_bytes")
     ws = torch.empty(need.value, dtype=torch.uint8, device=x.device)
-    with torch.cuda.device(dev):
-        rc = lib.dslpg_kernel_ff(xf.data_ptr(), w1c.data_ptr(), w3c.data_ptr(), rw.data_ptr(), out.data_ptr(), m, n, dim,
-                                 ws.data_ptr(), need.value, _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_kernel_ff")
+    _lib.launch(dev, "dslpg_kernel_ff", xf.data_ptr(), w1c.data_ptr(), w3c.data_ptr(), rw.data_ptr(), out.data_ptr(),
+                m, n, dim, ws.data_ptr(), need.value)
     return out.view(batch, seq_len, n)

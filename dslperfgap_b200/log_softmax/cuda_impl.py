@@ -31,8 +31,5 @@ def log_softmax(x, dim=-1, dtype=None):
     y = torch.empty(x.shape, dtype=out_dtype, device=x.device)
     if x.numel() == 0:
         return y
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_log_softmax_fwd(
-            x.data_ptr(), y.data_ptr(), m, n, k, in_code, out_code, _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_log_softmax_fwd")
+    _lib.launch(dev, "dslpg_log_softmax_fwd", x.data_ptr(), y.data_ptr(), m, n, k, in_code, out_code)
     return y

@@ -22,7 +22,5 @@ def logsumexp(x):
     if n == 0:
         return y.fill_(float("-inf"))  # logsumexp over an empty row
     m = y.numel()
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_logsumexp_fwd(x.data_ptr(), y.data_ptr(), m, n, code, _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_logsumexp_fwd")
+    _lib.launch(dev, "dslpg_logsumexp_fwd", x.data_ptr(), y.data_ptr(), m, n, code)
     return y

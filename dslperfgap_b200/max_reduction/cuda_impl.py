@@ -25,8 +25,5 @@ def max_reduction(input, dim, keepdim=False):
     indices = torch.empty(oshape, dtype=torch.int64, device=x.device)
     if values.numel() == 0:
         return (values, indices)
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_max_reduction(x.data_ptr(), values.data_ptr(), indices.data_ptr(), m, n, k, code,
-                                             _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_max_reduction")
+    _lib.launch(dev, "dslpg_max_reduction", x.data_ptr(), values.data_ptr(), indices.data_ptr(), m, n, k, code)
     return (values, indices)

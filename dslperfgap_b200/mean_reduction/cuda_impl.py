@@ -24,8 +24,6 @@ def mean_reduction(input_tensor, dim, keepdim=False, dtype=None):
         return y
     if n == 0:
         return y.fill_(float("nan"))  # torch: the mean of an empty set is NaN
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_mean_reduction(x.data_ptr(), y.data_ptr(), m, n, k, in_code,
-                                              _lib.FLOAT_CODES[out_dtype], _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_mean_reduction")
+    _lib.launch(dev, "dslpg_mean_reduction", x.data_ptr(), y.data_ptr(), m, n, k, in_code,
+                                              _lib.FLOAT_CODES[out_dtype])
     return y

@@ -32,10 +32,7 @@ def rms_norm(x, normalized_shape, weight, eps=1e-5):
     y = torch.empty_like(x)
     if x.numel() == 0:
         return y
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_rms_norm_fwd(
-            x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, xc, wc, float(eps), _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_rms_norm_fwd")
+    _lib.launch(dev, "dslpg_rms_norm_fwd", x.data_ptr(), w.data_ptr(), y.data_ptr(), m, n, xc, wc, float(eps))
     return y
 
 

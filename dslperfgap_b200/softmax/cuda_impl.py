@@ -17,7 +17,5 @@ def softmax(x):
         return y
     n = x.shape[-1] if x.dim() > 0 else 1
     m = x.numel() // n
-    with torch.cuda.device(dev):
-        rc = _lib.load().dslpg_softmax_fwd(x.data_ptr(), y.data_ptr(), m, n, code, _lib.stream_handle(dev))
-    _lib.check(rc, "dslpg_softmax_fwd")
+    _lib.launch(dev, "dslpg_softmax_fwd", x.data_ptr(), y.data_ptr(), m, n, code)
     return y

@@ -78,3 +78,18 @@ def test_argument_errors_return_before_launch(lib):
     # empty problems are a no-op success
     assert lib.dslpg_softmax_fwd(8, 8, 0, 4, 0, None) == 0
     assert lib.dslpg_logsumexp_fwd(8, 8, 0, 4, 0, None) == 0
+
+
+def test_fast_binding_matches_ctypes_signatures(lib):
+    """The METH_FASTCALL extension takes each entry point's arguments in the
+    ctypes order: all-NULL calls come back from the C layer as
+    DSLPG_ERR_NULL_POINTER (so arity and argument kinds agree)."""
+    fast = _lib.fast_module()
+    assert fast is not None, "the _dslpg_fast extension is not built"
+    names = [n for n in dir(fast) if n.startswith("dslpg_")]
+    assert len(names) >= 11
+    for name in names:
+        args = [0.0 if t is ctypes.c_float else 0 for t in _lib.SIGNATURES[name]]
+        assert getattr(fast, name)(*args) == -1, name
+        with pytest.raises(TypeError):
+            getattr(fast, name)(*args[:-1])
