@@ -4,7 +4,7 @@ Runs the reference's own PyTorch backend (tingxi-li/DSLPerfGap,
 ``ViperBench/<kernel>/pytorch_impl.py`` — the oracle its own test.py files
 compare every DSL backend against) on CPU, on seeded inputs, and stores inputs
 and outputs in ``golden_<op>.pt``. The reference checkout is read from
-``$DSLPG_REFERENCE`` (default: the read-only mount of this build container);
+``$DSLPG_REFERENCE`` (default: a `reference` directory beside this repository);
 the fixtures are committed, so nothing that runs on a GPU box needs it.
 
 Each case records:
@@ -34,7 +34,8 @@ from pathlib import Path
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("DSLPG_REFERENCE", "/root/reference")) / "ViperBench"
+# the reference checkout: DSLPG_REFERENCE, else a `reference` directory beside this repository
+REF = Path(os.environ.get("DSLPG_REFERENCE") or HERE.parents[2] / "reference") / "ViperBench"
 
 OPS = ["layer_norm", "rms_norm", "softmax", "log_softmax", "logsumexp", "cross_entropy", "cross_entropy_bwd",
        "mean_reduction", "max_reduction", "argmax", "linear_activation"]
