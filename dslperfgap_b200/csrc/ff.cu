@@ -175,7 +175,10 @@ struct FfArgs {
 // Tile order of the persistent grid: groups of up to kGroupM row tiles; inside
 // a group the row tile varies fastest, so the CTAs running at one time share a
 // few weight tiles (read from DRAM once) and the group's xs rows stay in L2.
-constexpr int kGroupM = 16;
+#ifndef DSLPG_FF_GROUP_M
+#define DSLPG_FF_GROUP_M 16
+#endif
+constexpr int kGroupM = DSLPG_FF_GROUP_M;
 
 DSLPG_DEV void tile_coords(int t, int mt, int nt, int& tm, int& tn) {
   const int per_group = kGroupM * nt;
@@ -496,6 +499,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFfThreads, 1)
           }
           const uint32_t st = ring + s * kStage2Bytes;
           const uint32_t fb = map_to_rank(full0 + 8u * s, 0);
+#ifdef DSLPG_FF_DIAG_NO_LOAD  // diagnostic builds only: after the first fill, MMAs re-read stale tiles
+          if (it >= kStages2) {
+            if (rank == 0) mbar_arrive(full0 + 8u * s);
+            continue;
+          }
+#endif
           if (rank == 0) mbar_arrive_expect_tx(full0 + 8u * s, 2 * kStage2Bytes);
           tma_load_2d_pair(st, &map_a, kb * kBK, arow, fb);
           tma_load_2d_pair(st + kTileA, map_b, kb * kBK, tn * kBN, fb);
