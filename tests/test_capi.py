@@ -75,6 +75,21 @@ def test_argument_errors_return_before_launch(lib):
     # eps
     assert lib.dslpg_layer_norm_fwd(8, 8, None, 8, 4, 4, 0, 0, float("nan"), None) == -4
     assert lib.dslpg_rms_norm_fwd(8, 8, 8, 4, 4, 0, 0, -1.0, None) == -4
+    # host-buffer rms_norm: nulls, dtype, eps, a missing workspace, the workspace size query
+    assert lib.dslpg_rms_norm_fwd_host(None, 8, 8, 4, 4, 2, 2, 1e-6, 8, 1 << 30, None) == -1
+    assert lib.dslpg_rms_norm_fwd_host(8, 8, 8, 4, 4, 2, 5, 1e-6, 8, 1 << 30, None) == -3
+    assert lib.dslpg_rms_norm_fwd_host(8, 8, 8, 4, 4, 2, 2, float("inf"), 8, 1 << 30, None) == -4
+    assert lib.dslpg_rms_norm_fwd_host(8, 8, 8, 4, 4, 2, 2, 1e-6, None, 1 << 30, None) == -1
+    need = ctypes.c_int64(-1)
+    assert lib.dslpg_rms_norm_fwd_host_workspace_bytes(16384, 8192, 2, ctypes.byref(need)) == 0
+    assert need.value == 4 * 2 * (16 << 20)  # 4 slots of a 16 MiB input chunk and its output chunk
+    assert lib.dslpg_rms_norm_fwd_host_workspace_bytes(3, 5, 0, ctypes.byref(need)) == 0 and need.value == 4 * 2 * 256
+    assert lib.dslpg_rms_norm_fwd_host(8, 8, 8, 4, 4, 2, 2, 1e-6, 256, need.value - 1, None) == -5  # too small
+    # kernel_ff: K % 8, the workspace size, and the static-scratch variant's limit (checked before M * K is formed)
+    assert lib.dslpg_kernel_ff(8, 8, 8, 8, 8, 4, 4, 12, 256, 1 << 20, None) == -2
+    assert lib.dslpg_kernel_ff(8, 8, 8, 8, 8, 4, 4, 16, 256, 1, None) == -5
+    assert lib.dslpg_kernel_ff_static(8, 8, 8, 8, 8, 1 << 30, 4, 1 << 30, None) == -6
+    assert lib.dslpg_kernel_ff_static(8, 8, 8, 8, 8, 2056, 4, 4096, None) == -6
     # empty problems are a no-op success
     assert lib.dslpg_softmax_fwd(8, 8, 0, 4, 0, None) == 0
     assert lib.dslpg_logsumexp_fwd(8, 8, 0, 4, 0, None) == 0
