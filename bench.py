@@ -422,7 +422,9 @@ def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler
         "ms_per_step": round(ms_step, 5), "median_ms": round(statistics.median(per), 5),
         "gbs": round(agg_gbs, 1), "gbs_per_gpu": round(achieved, 1),
         "frac_measured": round(achieved / peak, 4), "frac_spec": round(achieved / SPEC_HBM_GBS, 4),
-        "algo_bytes_per_launch": bytes_rank, "launches": steps,
+        "algo_bytes_per_launch": bytes_rank,
+        # kernels of this backend launched in the timed steps (kernel_ff: row pass + GEMM)
+        "launches": steps * (2 if cfg.op == "linear_activation" else 1),
     })
     if with_torch:
         label, fn = torch_baseline(wl)
@@ -481,7 +483,9 @@ def measure_e2e(name, rank, world, dev, timer, steps, warmup):
             "ms_per_step": round(t_max / steps, 4),
             "path": "dslperfgap_b200.rms_norm_host (public API) -> dslpg_rms_norm_fwd_host, pinned host buffers, "
                     "16 MiB chunks with uploads, kernels and downloads overlapped",
-            "result_matches_device_path": bool(ok)}
+            "result_matches_device_path": bool(ok),
+            # one RMSNorm kernel per 16 MiB chunk of input rows
+            "launches": steps * -(-x_host.numel() * x_host.element_size() // (16 << 20))}
 
 
 # ------------------------------------------------- the reference's large shapes
@@ -757,7 +761,7 @@ def main(argv=None):
             "e2e": e2e,
             "kernel_path": args.path,
             "wait_timeouts": L.take_wait_timeouts(),
-            "gpu_launches": sum(k["launches"] for k in kernels.values()) + (e2e_steps if e2e else 0),
+            "gpu_launches": sum(k["launches"] for k in kernels.values()) + (e2e["launches"] if e2e else 0),
             "clocks": clocks,
             "kernels": kernels,
             "reference_shapes": ref_shapes,
