@@ -107,6 +107,7 @@ def measured_tensor_peak():
 
 
 TENSOR_PEAK = measured_tensor_peak()
+ROWS_OVERRIDE = 0  # --rows: measure the first R rows of a workload (small profiling captures)
 
 
 def profile_traffic():
@@ -298,6 +299,16 @@ def direct_launcher(wl, dev):
         keep = [y, ws]
         f = lambda: lib.dslpg_kernel_ff(x.data_ptr(), w1.data_ptr(), w3.data_ptr(), rw.data_ptr(), y.data_ptr(), M,
                                         cfg.N, cfg.K, ws.data_ptr(), need.value, stream)
+    elif cfg.op == "cross_entropy_fwd_bwd":
+        k = wl.kwargs
+        x, labels, dloss = a
+        outs = [torch.empty(M, dtype=torch.float32, device=dev) for _ in range(3)]
+        y = torch.empty_like(x)
+        keep = outs + [y]
+        f = lambda: lib.dslpg_cross_entropy_fwd_bwd(
+            x.data_ptr(), labels.data_ptr(), dloss.data_ptr(), _lib.F32, 1, outs[0].data_ptr(), outs[1].data_ptr(),
+            outs[2].data_ptr(), y.data_ptr(), M, N, N, N, code, _lib.I64, k["smoothing"], k["logit_scale"],
+            k["lse_square_scale"], k["ignored_index"], float(k["total_classes"]), k["class_start_idx"], 0, stream)
     elif cfg.op == "cross_entropy_bwd":
         k = wl.kwargs
         dloss, x, lse, labels = a
@@ -352,6 +363,17 @@ def torch_baseline(wl):
         return "torch.max(dim)", lambda: torch.max(a[0], 1)
     if cfg.op == "argmax":
         return "torch.argmax", lambda: torch.argmax(a[0], 1)
+    if cfg.op == "cross_entropy_fwd_bwd":
+        # torch's fused cross-entropy forward and its autograd backward with the same dloss
+        import torch.nn.functional as F
+        x, labels, dloss = a
+
+        def fwd_bwd():
+            xl = x.detach().requires_grad_(True)
+            loss = F.cross_entropy(xl, labels, ignore_index=-100, reduction="none")
+            loss.backward(dloss)
+            return loss, xl.grad
+        return "F.cross_entropy + autograd backward", fwd_bwd
     if cfg.op == "cross_entropy_bwd":
         # the vectorised eager form of pytorch_impl.cross_entropy_bwd (its own
         # Python loop is not a GPU baseline)
@@ -396,6 +418,8 @@ def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler
     cfg = workloads.CONFIGS[name]
     sharded = name == "layer_norm_bf16_sharded"
     rows = workloads.shard_rows(cfg.M, rank, world) if sharded else None
+    if ROWS_OVERRIDE and not sharded:
+        rows = (0, min(ROWS_OVERRIDE, cfg.M))
     wl = workloads.make(name, seed=0, device=dev, rows=rows)
     launch = direct_launcher(wl, dev)
     per = timer.time_steps(launch, steps, warmup, sampler)
@@ -442,6 +466,19 @@ def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler
             t_e = timer.max_over_ranks(sum(te)) / steps
             res["torch_eager_pytorch_impl_ms"] = round(t_e, 5)
             res["e_lib_vs_pytorch_impl_pct"] = round(100.0 * t_e / ms_step, 1)
+        if cfg.op == "cross_entropy_fwd_bwd":
+            # this backend's own forward (one block per row) followed by its backward, same inputs
+            import dslperfgap_b200 as B
+            x, labels, dloss = wl.args
+            kw = dict(wl.kwargs)
+
+            def separate():
+                _, lse, _ = B.cross_entropy_fwd(x, labels, **kw, BLOCK_SIZE=cfg.N, SPLIT=False)
+                B.cross_entropy_bwd(dloss, x, lse.view(-1)[:x.shape[0]], labels, **kw, BLOCK_SIZE=cfg.N)
+            ts = timer.time_steps(separate, steps, warmup)
+            t_s = timer.max_over_ranks(sum(ts)) / steps
+            res["separate_fwd_then_bwd_ms"] = round(t_s, 5)
+            res["fused_vs_separate_pct"] = round(100.0 * t_s / ms_step, 1)
         if cfg.op == "linear_activation":
             # the GEMM alone through cuBLAS: xs @ [w1; w3]^T, fp16 (no norm, no gate)
             xs = (wl.args[0].reshape(-1, cfg.K) * wl.args[3]).contiguous()
@@ -684,6 +721,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--workload", default=HEADLINE, choices=workloads.NAMES)
     ap.add_argument("--headline-only", action="store_true", help="skip the other configurations")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="use only the first ROWS rows of the workload(s) (for small ncu captures; not a bench line)")
     ap.add_argument("--no-reference-shapes", action="store_true",
                     help="skip the reference's large benchmark shapes (timed with its protocol)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -694,6 +733,8 @@ def main(argv=None):
                     help="time only this backend's kernels (no torch baselines, e2e or CPU baseline); "
                          "used for profiling")
     args = ap.parse_args(argv)
+    global ROWS_OVERRIDE
+    ROWS_OVERRIDE = args.rows
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()
     keep_stdout_for_result()

@@ -42,6 +42,9 @@ SIGNATURES = {
         _vp, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
         _c_f32, _c_f32, _c_f32, _c_i64, _c_f32, _c_i64, _c_int, _vp,
     ],
+    "dslpg_cross_entropy_fwd_bwd": [_vp, _vp, _vp, _c_int, _c_i64, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
+                                    _c_i64, _c_int, _c_int, _c_f32, _c_f32, _c_f32, _c_i64, _c_f32, _c_i64, _c_int,
+                                    _vp],
     "dslpg_mean_reduction": [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
     "dslpg_max_reduction": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "dslpg_argmax": [_vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],

@@ -75,6 +75,11 @@ ENTRY(dslpg_cross_entropy_bwd, "pllppppllllllffflfllp",
       dslpg_cross_entropy_bwd(v[0].p, (int)v[1].l, v[2].l, v[3].p, (const float*)v[4].p, v[5].p, v[6].p, v[7].l,
                               v[8].l, v[9].l, v[10].l, (int)v[11].l, (int)v[12].l, v[13].f, v[14].f, v[15].f, v[16].l,
                               v[17].f, v[18].l, (int)v[19].l, STREAM(v[20])))
+ENTRY(dslpg_cross_entropy_fwd_bwd, "ppplpppppllllllffflfllp",
+      dslpg_cross_entropy_fwd_bwd(v[0].p, v[1].p, v[2].p, (int)v[3].l, v[4].l, (float*)v[5].p, (float*)v[6].p,
+                                  (float*)v[7].p, v[8].p, v[9].l, v[10].l, v[11].l, v[12].l, (int)v[13].l,
+                                  (int)v[14].l, v[15].f, v[16].f, v[17].f, v[18].l, v[19].f, v[20].l, (int)v[21].l,
+                                  STREAM(v[22])))
 ENTRY(dslpg_mean_reduction, "pplllllp",
       dslpg_mean_reduction(v[0].p, v[1].p, v[2].l, v[3].l, v[4].l, (int)v[5].l, (int)v[6].l, STREAM(v[7])))
 ENTRY(dslpg_max_reduction, "ppplllip",
@@ -88,7 +93,8 @@ static PyMethodDef methods[] = {
     M(dslpg_layer_norm_fwd), M(dslpg_rms_norm_fwd),      M(dslpg_softmax_fwd),
     M(dslpg_log_softmax_fwd), M(dslpg_logsumexp_fwd),    M(dslpg_cross_entropy_fwd),
     M(dslpg_cross_entropy_bwd), M(dslpg_mean_reduction), M(dslpg_max_reduction),
-    M(dslpg_argmax),          M(dslpg_kernel_ff),        {NULL, NULL, 0, NULL}};
+    M(dslpg_argmax),          M(dslpg_kernel_ff),        M(dslpg_cross_entropy_fwd_bwd),
+    {NULL, NULL, 0, NULL}};
 
 static struct PyModuleDef module = {PyModuleDef_HEAD_INIT, "_dslpg_fast",
                                     "METH_FASTCALL bindings of libdslpg_b200's per-call entry points", -1, methods,

@@ -225,7 +225,10 @@ cudaError_t launch_rows(RedArgs a, cudaStream_t st) {
   // Vectors per thread per row: max / argmax pay a fixed per-row cost (the
   // 64-bit index merge and the re-read of the winning chunk), so they take
   // longer slices.
-  const int64_t per_thread = (V > 1) ? (OP == kMean ? 16 : 64) : 64;
+#ifndef DSLPG_RED_PER_THREAD_MAX
+#define DSLPG_RED_PER_THREAD_MAX 64
+#endif
+  const int64_t per_thread = (V > 1) ? (OP == kMean ? 16 : DSLPG_RED_PER_THREAD_MAX) : 64;
   int64_t want = (units + per_thread - 1) / per_thread;
   int tpr = static_cast<int>(want > 256 ? 256 : want);
   tpr = round_up32(tpr < 32 ? 32 : tpr);
@@ -233,7 +236,11 @@ cudaError_t launch_rows(RedArgs a, cudaStream_t st) {
   a.rpc = tpr >= 256 ? 1 : 256 / tpr;
   const int block = a.tpr * a.rpc;
   const void* fn = reinterpret_cast<const void*>(&reduce_rows_kernel<OP, Tin, Tout, V, MINB>);
+#ifdef DSLPG_RED_NONPERSISTENT
+  const int grid = static_cast<int>((a.M + a.rpc - 1) / a.rpc);
+#else
   const int grid = persistent_grid(fn, block, 0, (a.M + a.rpc - 1) / a.rpc);
+#endif
   reduce_rows_kernel<OP, Tin, Tout, V, MINB><<<grid, block, 0, st>>>(a);
   return cudaGetLastError();
 }
@@ -250,7 +257,10 @@ cudaError_t launch_red(RedArgs a, cudaStream_t st) {
   if (aligned(a.x, 16) && a.N % E == 0 && a.N / E <= 0x7fffffff) {
     a.nvec = static_cast<int>(a.N / E);
     // max / argmax: registers bounded to four CTAs per SM (measured faster)
-    if constexpr (OP != kMean) return launch_rows<OP, Tin, Tout, E, 4>(a, st);
+#ifndef DSLPG_RED_MINB_MAX
+#define DSLPG_RED_MINB_MAX 4
+#endif
+    if constexpr (OP != kMean) return launch_rows<OP, Tin, Tout, E, DSLPG_RED_MINB_MAX>(a, st);
     return launch_rows<OP, Tin, Tout, E>(a, st);
   }
   return launch_rows<OP, Tin, Tout, 1>(a, st);

@@ -16,6 +16,7 @@
 // ViperBench/cross_entropy/triton_impl.py:46,75-76.
 #include "common.cuh"
 #include "pipe.cuh"
+#include "xent_grad.cuh"
 
 namespace dslpg {
 
@@ -246,6 +247,120 @@ __global__ void __launch_bounds__(256, MINB) rowstat_kernel(const StatArgs a) {
     }
 
     if (t == 0 && iv) finish_item<KIND, T, SMOOTH>(a, r, cb, col0, gm, gs, gsum);
+  }
+}
+
+// Cross-entropy forward and backward in one kernel, for a row that is one
+// column block (BLOCK_SIZE >= n_cols) and a dloss known before the forward
+// (a mean or sum of the losses). One CTA of fused_threads() per row, one CTA per
+// SM: pass 1 streams the row from HBM into the online statistics (as
+// rowstat_kernel) and writes loss / lse / z_loss; pass 2 reads the row again,
+// now from L2 (the rows in flight take about 250 KiB each, 148 of them well
+// inside the 126 MB L2), and writes dlogits with the backward's arithmetic.
+// HBM traffic: the logits once and dlogits once, against the logits twice for
+// a forward followed by a backward. Pass 1 reads with an L2 evict-last policy.
+DSLPG_DEV Vec16 ld_policy(const void* p, uint64_t pol) {
+  Vec16 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+      : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+struct FusedArgs {
+  StatArgs s;
+  const void* dloss;
+  int dloss_dt;
+  int64_t dloss_stride;
+  void* dx;
+  int64_t ldo;
+  int nvec;  // N / V on the vector path
+};
+
+// Threads per row: 1024; 512 with smoothing, whose extra sum of the logits
+// does not fit the 64 registers a thread has at 1024 threads.
+#ifndef DSLPG_FUSED_CTAS
+#define DSLPG_FUSED_CTAS 1  // CTAs per SM
+#endif
+template <bool SMOOTH>
+constexpr int fused_threads() {
+  return (SMOOTH ? 512 : 1024) / DSLPG_FUSED_CTAS;
+}
+
+template <typename T, int V, bool SMOOTH>
+__global__ void __launch_bounds__(fused_threads<SMOOTH>(), DSLPG_FUSED_CTAS) xent_fused_kernel(const FusedArgs f) {
+  constexpr int U = 4;
+  constexpr int kFusedThreads = fused_threads<SMOOTH>();
+  const StatArgs& a = f.s;
+  __shared__ float red[2][32];
+  const int t = threadIdx.x, nw = kFusedThreads / 32;
+  int buf = 0;
+  for (int64_t r = blockIdx.x; r < a.M; r += gridDim.x) {
+    const T* xr = static_cast<const T*>(a.x) + r * a.ld;
+    float m = kNegInf, s = 0.f, sum = 0.f;
+    // pass 1 marks the row's lines evict-last so that pass 2 finds them in L2
+    // (without the hint it read about 1.8x the logits from DRAM)
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    if constexpr (V > 1) {
+      const int64_t nv = f.nvec, stride = static_cast<int64_t>(U) * kFusedThreads;
+      auto load = [&](Vec16 (&dst)[U], int64_t j0) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t j = j0 + static_cast<int64_t>(u) * kFusedThreads;
+          dst[u] = Vec16{{0u, 0u, 0u, 0u}};
+          if (j < nv) dst[u] = ld_policy(xr + j * V, pol);
+        }
+      };
+      Vec16 nx[U];
+      load(nx, t);
+      for (int64_t j0 = t; j0 < nv; j0 += stride) {
+        Vec16 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = nx[u];
+        if (j0 + stride < nv) load(nx, j0 + stride);
+        bool ok[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) ok[u] = j0 + static_cast<int64_t>(u) * kFusedThreads < nv;
+        if (ok[U - 1]) fold_vecs<T, U, SMOOTH, 4>(m, s, sum, v, a.c);
+        else fold_vecs_masked<T, U, SMOOTH>(m, s, sum, v, ok, a.c);
+      }
+    } else {
+      for (int64_t j0 = t; j0 < a.N; j0 += static_cast<int64_t>(U) * kFusedThreads) {
+        float tv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t j = j0 + static_cast<int64_t>(u) * kFusedThreads;
+          float x = 0.f;
+          if (j < a.N) x = to_f(xr[j]);
+          if constexpr (SMOOTH) sum += x;
+          tv[u] = (j < a.N) ? x * a.c : kNegInf;
+        }
+        fold_chunk<U>(m, s, tv);
+      }
+    }
+    const float gm = group_reduce<MaxOp>(m, red[buf], nw, 0);
+    buf ^= 1;
+    const float gs = group_reduce<SumOp>((m == gm) ? s : s * ex2(m - gm), red[buf], nw, 0);
+    buf ^= 1;
+    float gsum = 0.f;
+    if constexpr (SMOOTH) {
+      gsum = group_reduce<SumOp>(sum, red[buf], nw, 0);
+      buf ^= 1;
+    }
+    if (t == 0) finish_item<kXent, T, SMOOTH>(a, r, 0, 0, gm, gs, gsum);
+    // the lse finish_item stored, formed the same way by every thread
+    const float lse = (fabsf(gm) < kPosInf) ? (gm + log2f(gs)) * kLn2 : kNaN;
+    const int64_t label = a.label64 ? static_cast<const int64_t*>(a.labels)[r]
+                                    : static_cast<int64_t>(static_cast<const int32_t*>(a.labels)[r]);
+    const float dl = (label != a.ignored) ? load_any(f.dloss, r * f.dloss_stride, f.dloss_dt) : 0.f;
+    const GradRow b =
+        grad_row_consts(dl, a.scale, lse, a.lse_sq, SMOOTH, a.smoothing, a.total_classes, label, a.class_start);
+#ifdef DSLPG_FUSED_PASS2_EVICT_FIRST
+    grad_row<T, V, true>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH, t, kFusedThreads);
+#else
+    grad_row<T, V>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH, t, kFusedThreads);
+#endif
   }
 }
 
@@ -517,6 +632,32 @@ cudaError_t dispatch_dtype(StatArgs a, int dt, cudaStream_t st) {
   }
 }
 
+template <typename T, bool SMOOTH>
+cudaError_t launch_fused_t(FusedArgs f, cudaStream_t st) {
+  constexpr int E = Elt<T>::kPerVec;
+  const bool vec = aligned(f.s.x, 16) && aligned(f.dx, 16) && f.s.N % E == 0 && f.s.ld % E == 0 && f.ldo % E == 0 &&
+                   f.s.N / E <= 0x7fffffff;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * DSLPG_FUSED_CTAS;  // rows in flight stay in L2
+  const int64_t rows = f.s.M < cap ? f.s.M : cap;
+  if (vec) {
+    f.nvec = static_cast<int>(f.s.N / E);
+    xent_fused_kernel<T, E, SMOOTH><<<static_cast<int>(rows), fused_threads<SMOOTH>(), 0, st>>>(f);
+  } else {
+    f.nvec = 0;
+    xent_fused_kernel<T, 1, SMOOTH><<<static_cast<int>(rows), fused_threads<SMOOTH>(), 0, st>>>(f);
+  }
+  return cudaGetLastError();
+}
+
+template <bool SMOOTH>
+cudaError_t launch_fused(FusedArgs f, int dt, cudaStream_t st) {
+  switch (dt) {
+    case DSLPG_F32: return launch_fused_t<float, SMOOTH>(f, st);
+    case DSLPG_F16: return launch_fused_t<__half, SMOOTH>(f, st);
+    default: return launch_fused_t<__nv_bfloat16, SMOOTH>(f, st);
+  }
+}
+
 }  // namespace
 }  // namespace dslpg
 
@@ -589,3 +730,46 @@ unsigned int take_wait_timeouts_rowstat() {
   return v;
 }
 }  // namespace dslpg
+
+extern "C" int dslpg_cross_entropy_fwd_bwd(const void* logits, const void* labels, const void* dloss, int dloss_dtype,
+                                           int64_t dloss_stride, float* loss, float* lse, float* z_loss,
+                                           void* dlogits, int64_t n_rows, int64_t n_cols, int64_t logits_row_stride,
+                                           int64_t dlogits_row_stride, int logits_dtype, int labels_dtype,
+                                           float smoothing, float logit_scale, float lse_square_scale,
+                                           int64_t ignored_index, float total_classes, int64_t class_start_idx,
+                                           int has_smoothing, cudaStream_t stream) {
+  if (!logits || !labels || !dloss || !loss || !lse || !z_loss || !dlogits) return DSLPG_ERR_NULL_POINTER;
+  if (n_rows < 0 || n_cols < 0 || logits_row_stride < n_cols || dlogits_row_stride < n_cols || dloss_stride < 0)
+    return DSLPG_ERR_BAD_SHAPE;
+  if (!is_float_dtype(logits_dtype) || !is_float_dtype(dloss_dtype)) return DSLPG_ERR_BAD_DTYPE;
+  if (labels_dtype != DSLPG_I32 && labels_dtype != DSLPG_I64) return DSLPG_ERR_BAD_DTYPE;
+  if (n_rows == 0 || n_cols == 0) return DSLPG_OK;
+  FusedArgs f{};
+  StatArgs& a = f.s;
+  a.x = logits;
+  a.M = n_rows;
+  a.N = n_cols;
+  a.ld = logits_row_stride;
+  a.seg = n_cols;
+  a.nseg = 1;
+  a.c = logit_scale * kLog2e;
+  a.labels = labels;
+  a.label64 = labels_dtype == DSLPG_I64 ? 1 : 0;
+  a.loss = loss;
+  a.lse = lse;
+  a.zloss = z_loss;
+  a.smoothing = smoothing;
+  a.scale = logit_scale;
+  a.lse_sq = lse_square_scale;
+  a.total_classes = total_classes;
+  a.ignored = ignored_index;
+  a.class_start = class_start_idx;
+  a.split = 0;
+  f.dloss = dloss;
+  f.dloss_dt = dloss_dtype;
+  f.dloss_stride = dloss_stride;
+  f.dx = dlogits;
+  f.ldo = dlogits_row_stride;
+  cudaError_t e = has_smoothing ? launch_fused<true>(f, logits_dtype, stream) : launch_fused<false>(f, logits_dtype, stream);
+  return static_cast<int>(e);
+}

@@ -16,6 +16,7 @@ each output written once:
   logsumexp                                      M * N * elem_size + M * elem_size
   cross_entropy (one block per row)              M * N * elem_size + 8 * M + 3 * 4 * M
   cross_entropy_bwd                              2 * M * N * elem_size + 8 * M + 4 * M + 4 * M
+  cross_entropy_fwd_bwd                          2 * M * N * elem_size + 8 * M + 4 * M + 3 * 4 * M
   mean_reduction / max_reduction / argmax        M * N * elem_size + the M outputs
   linear_activation (kernel_ff)                  (M*K + 2*N*K + K + M*N) * 2; its roofline is
                                                  tensor-bound: 4 * M * N * K flops
@@ -70,6 +71,13 @@ CONFIGS = {
                "U[0,128256), 410 rows ignore_index=-100, dloss~U(0.5,1.5), lse = row logsumexp",
                dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.0, ignored_index=-100,
                     total_classes=128256, class_start_idx=0, BLOCK_SIZE=131072, HAS_SMOOTHING=False)),
+        Config("cross_entropy_fwd_bwd_bf16", "cross_entropy_fwd_bwd", "cross_entropy_fwd_bwd", 8192, 128256,
+               torch.bfloat16,
+               "cross-entropy forward + backward in one pass, bf16, on the forward's configuration: "
+               "logits[8192,128256]~N(0,2), int64 targets U[0,128256), 410 rows ignore_index=-100, "
+               "dloss = 1/n_valid (the gradient of the mean loss)",
+               dict(smoothing=0.0, logit_scale=1.0, lse_square_scale=0.0, ignored_index=-100,
+                    total_classes=128256, class_start_idx=0, HAS_SMOOTHING=False)),
         Config("mean_reduction_fp32", "mean_reduction", "mean_reduction", 8192, 32768, torch.float32,
                "mean over dim 1, fp32 x[8192,32768]~N(0,1) (the reference's large shape, benchmark.py:288-290)",
                {"dim": 1}),
@@ -148,6 +156,8 @@ def algo_bytes(cfg: Config, rows: int) -> int:
         return rows * cfg.N * es + 8 * rows + 3 * 4 * rows
     if cfg.op == "cross_entropy_bwd":
         return 2 * rows * cfg.N * es + 8 * rows + 4 * rows + 4 * rows
+    if cfg.op == "cross_entropy_fwd_bwd":  # logits read once, dlogits written, labels + dloss, 3 fp32 outputs
+        return 2 * rows * cfg.N * es + 8 * rows + 4 * rows + 3 * 4 * rows
     if cfg.op == "mean_reduction":
         return rows * cfg.N * es + rows * es
     if cfg.op == "max_reduction":
@@ -232,7 +242,7 @@ def make(name: str, seed: int = 0, device="cpu", rows: tuple | None = None) -> W
         args = [x.reshape(1, r1 - r0, cfg.K), w1, w3, rw]
     elif cfg.op in ("mean_reduction", "max_reduction", "argmax"):
         args = [_rows(cfg, r0, r1, seed, device, 1.0, False)]
-    elif cfg.op in ("cross_entropy", "cross_entropy_bwd"):
+    elif cfg.op in ("cross_entropy", "cross_entropy_bwd", "cross_entropy_fwd_bwd"):
         x = _rows(cfg, r0, r1, seed, device, 2.0, False)
         g = _gen("cpu", seed + 103)
         labels = torch.randint(0, cfg.N, (cfg.M,), generator=g, dtype=torch.int64)
@@ -241,6 +251,9 @@ def make(name: str, seed: int = 0, device="cpu", rows: tuple | None = None) -> W
         labels = labels[r0:r1].to(device)
         if cfg.op == "cross_entropy":
             args = [x, labels]
+        elif cfg.op == "cross_entropy_fwd_bwd":
+            dloss = torch.full((r1 - r0,), 1.0 / (cfg.M - n_ign), dtype=torch.float32, device=device)
+            args = [x, labels, dloss]
         else:
             dloss = (torch.rand(cfg.M, generator=g) + 0.5)[r0:r1].to(device)
             # input preparation only: the forward's per-row lse

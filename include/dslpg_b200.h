@@ -173,6 +173,26 @@ DSLPG_API int dslpg_cross_entropy_bwd(const void* dloss, int dloss_dtype, int64_
                             int has_smoothing, cudaStream_t stream);
 
 /*
+ * Cross-entropy forward and backward in one pass over the logits, for one
+ * column block per row (the reference's BLOCK_SIZE >= n_cols) without SPLIT,
+ * when dloss is known before the forward (the gradient of a mean or sum of
+ * the per-row losses). loss / lse / z_loss: [n_rows] fp32, the values
+ * dslpg_cross_entropy_fwd stores at flat index r; dlogits as
+ * dslpg_cross_entropy_bwd computes them from that lse. The logits are read
+ * from HBM once (the second pass over a row hits L2) instead of twice.
+ * Serves cross_entropy_fwd followed by cross_entropy_bwd of
+ * ViperBench/cross_entropy/triton_impl.py:123-140 and :79-120
+ * (pytorch_impl.py:4-90 and :93-141).
+ */
+DSLPG_API int dslpg_cross_entropy_fwd_bwd(const void* logits, const void* labels, const void* dloss, int dloss_dtype,
+                                          int64_t dloss_stride, float* loss, float* lse, float* z_loss, void* dlogits,
+                                          int64_t n_rows, int64_t n_cols, int64_t logits_row_stride,
+                                          int64_t dlogits_row_stride, int logits_dtype, int labels_dtype,
+                                          float smoothing, float logit_scale, float lse_square_scale,
+                                          int64_t ignored_index, float total_classes, int64_t class_start_idx,
+                                          int has_smoothing, cudaStream_t stream);
+
+/*
  * Reductions over the middle axis of a dense [M, N, K] tensor (a reduced run
  * of adjacent axes is one N; K == 1 reduces rows). Index outputs are int64 and
  * follow torch: the first NaN is the maximum; equal maxima give the smallest

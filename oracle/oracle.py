@@ -186,6 +186,20 @@ def cross_entropy_bwd(dloss, logits, lse, labels, smoothing, logit_scale, lse_sq
     return dx
 
 
+def cross_entropy_fwd_bwd(logits, labels, dloss, smoothing, logit_scale, lse_square_scale,
+                          ignored_index, total_classes, class_start_idx, HAS_SMOOTHING):
+    """cross_entropy_fwd with one block per row (BLOCK_SIZE = C, SPLIT False)
+    followed by cross_entropy_bwd from that lse (the same two reference
+    functions): (loss, lse, z_loss) as 1-D [R], and dlogits."""
+    c = _host(logits).shape[1]
+    kw = dict(smoothing=smoothing, logit_scale=logit_scale, lse_square_scale=lse_square_scale,
+              ignored_index=ignored_index, total_classes=total_classes, class_start_idx=class_start_idx)
+    loss, lse, z = cross_entropy_fwd(logits, labels, **kw, BLOCK_SIZE=max(c, 1), HAS_SMOOTHING=HAS_SMOOTHING,
+                                     SPLIT=False, valid_only=True)
+    dx = cross_entropy_bwd(dloss, logits, lse, labels, **kw, BLOCK_SIZE=max(c, 1), HAS_SMOOTHING=HAS_SMOOTHING)
+    return loss, lse, z, dx
+
+
 def _mnk(x, dims):
     """(contiguous x, M, N, K, output shape without keepdim) for reducing `dims`."""
     shape = tuple(x.shape) if x.dim() else (1,)

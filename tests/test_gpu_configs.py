@@ -29,6 +29,10 @@ def test_full_size_config_matches_oracle(name):
         nv = wl.valid_entries
         for i, (o, r) in enumerate(zip(out, ref)):
             assert_parity(o.reshape(-1)[:nv], r.reshape(-1)[:nv], torch.float32)
+    elif wl.op == "cross_entropy_fwd_bwd":  # (loss, lse, z_loss) [M] and dlogits
+        for o, r in zip(out[:3], ref[:3]):
+            assert_parity(o, r, torch.float32)
+        assert_parity(out[3], ref[3], wl.config.dtype)
     elif isinstance(ref, tuple):  # max_reduction: (values, indices)
         assert_parity(out[0], ref[0], ref[0].dtype)
         assert torch.equal(out[1].cpu(), ref[1])
