@@ -356,11 +356,11 @@ __global__ void __launch_bounds__(fused_threads<SMOOTH>(), DSLPG_FUSED_CTAS) xen
     const float dl = (label != a.ignored) ? load_any(f.dloss, r * f.dloss_stride, f.dloss_dt) : 0.f;
     const GradRow b =
         grad_row_consts(dl, a.scale, lse, a.lse_sq, SMOOTH, a.smoothing, a.total_classes, label, a.class_start);
-#ifdef DSLPG_FUSED_PASS2_EVICT_FIRST
-    grad_row<T, V, true>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH, t, kFusedThreads);
-#else
-    grad_row<T, V>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH, t, kFusedThreads);
+#ifndef DSLPG_FUSED_PASS2_U
+#define DSLPG_FUSED_PASS2_U 4
 #endif
+    grad_row<T, V, false, DSLPG_FUSED_PASS2_U>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH,
+                                               t, kFusedThreads);
   }
 }
 

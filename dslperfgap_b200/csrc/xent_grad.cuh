@@ -51,10 +51,10 @@ DSLPG_DEV float grad_elem(const GradRow& b, float x, float scale, bool is_label,
 // column is rewritten afterwards by the thread that wrote its vector, so it is
 // ordered after that thread's own vector store.
 // LAST_USE: the row's loads carry an L2 evict-first policy (its last read).
-template <typename T, int V, bool LAST_USE = false>
+// U: 16-byte loads in flight per thread.
+template <typename T, int V, bool LAST_USE = false, int U = 4>
 DSLPG_DEV void grad_row(const T* xr, T* yr, int nvec, int64_t N, const GradRow& b, float scale, bool smooth, int t,
                         int tpr) {
-  constexpr int U = 4;
   if constexpr (V > 1) {
     constexpr int P = V / 2;
     const f32x2 nl2 = pk2(-b.lse * kLog2e, -b.lse * kLog2e);
