@@ -61,8 +61,6 @@ DSLPG_DEV void fold_chunk(float& m, float& s, const float* t) {
   m = nm;
 }
 
-// Write the results of work item (row r, block cb) from the merged online
-// statistics: gm = max of t, gs = sum of 2^(t - gm), gsum = sum of x (SMOOTH).
 // Fold NV full 16-byte vectors of T (every element valid) into the running
 // (m, s) of t = x * c in the log2 domain; with SMOOTH also add the plain sum of
 // x to `sum`. The chunk's extreme is found on the stored values (two 16-bit
@@ -126,9 +124,33 @@ DSLPG_DEV void fold_vecs_masked(float& m, float& s, float& sum, const Vec16 (&v)
   fold_chunk<NV * E>(m, s, tv);
 }
 
+// The label of row r and, when it falls in the block [col0, hi), its scaled
+// logit: loaded when the item starts, so the two dependent loads overlap the
+// item's stream instead of following it.
+struct LabelPick {
+  int64_t label;
+  float xl;      // logit[label] * scale (0 when the label is not in the block)
+  bool in_block;
+};
+
+template <typename T>
+DSLPG_DEV LabelPick pick_label(const StatArgs& a, int64_t r, int64_t cb, int64_t col0) {
+  LabelPick p;
+  p.label = a.label64 ? static_cast<const int64_t*>(a.labels)[r]
+                      : static_cast<int64_t>(static_cast<const int32_t*>(a.labels)[r]);
+  const int64_t adj = p.label - a.class_start;
+  const int64_t hi = (cb + 1) * a.seg < a.N ? (cb + 1) * a.seg : a.N;
+  p.in_block = p.label != a.ignored && adj >= col0 && adj < hi;
+  p.xl = p.in_block ? to_f(static_cast<const T*>(a.x)[r * a.ld + adj]) * a.scale : 0.f;
+  return p;
+}
+
+// Write the results of work item (row r, block cb) from the merged online
+// statistics: gm = max of t, gs = sum of 2^(t - gm), gsum = sum of x (SMOOTH),
+// and (cross-entropy) the item's label pick.
 template <int KIND, typename T, bool SMOOTH>
-DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col0, float gm, float gs,
-                           float gsum) {
+DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, float gm, float gs, float gsum,
+                           const LabelPick& lp) {
   const float lse_fin = (gm + log2f(gs)) * kLn2;
   if constexpr (KIND == kLse) {
     // torch.logsumexp shifts by the max only when it is finite.
@@ -140,20 +162,15 @@ DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col
     const float lse = (fabsf(gm) < kPosInf) ? lse_fin : kNaN;
     const int64_t oi = cb * a.M + r;
     a.lse[oi] = lse;
-    const int64_t label = a.label64 ? static_cast<const int64_t*>(a.labels)[r]
-                                    : static_cast<int64_t>(static_cast<const int32_t*>(a.labels)[r]);
     float loss = 0.f, z = 0.f;
-    if (label != a.ignored) {
-      const int64_t adj = label - a.class_start;
+    if (lp.label != a.ignored) {
       const float lse_term = a.split ? 0.f : lse;
       const float sum_logits = gsum * a.scale;
-      const int64_t hi = (cb + 1) * a.seg < a.N ? (cb + 1) * a.seg : a.N;
-      if (adj >= col0 && adj < hi) {
-        const float xl = to_f(static_cast<const T*>(a.x)[r * a.ld + adj]) * a.scale;
+      if (lp.in_block) {
         if constexpr (SMOOTH)
-          loss = lse_term - a.smoothing * sum_logits / a.total_classes - (1.f - a.smoothing) * xl;
+          loss = lse_term - a.smoothing * sum_logits / a.total_classes - (1.f - a.smoothing) * lp.xl;
         else
-          loss = lse_term - xl;
+          loss = lse_term - lp.xl;
       } else if constexpr (SMOOTH) {
         loss = a.smoothing * (lse_term - sum_logits / a.total_classes);
       }
@@ -165,6 +182,15 @@ DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col
     a.loss[oi] = loss;
     a.zloss[oi] = z;
   }
+}
+
+// finish_item with the label loaded at the end (kernels that do not prefetch it).
+template <int KIND, typename T, bool SMOOTH>
+DSLPG_DEV void finish_item(const StatArgs& a, int64_t r, int64_t cb, int64_t col0, float gm, float gs,
+                           float gsum) {
+  LabelPick lp{0, 0.f, false};
+  if constexpr (KIND == kXent) lp = pick_label<T>(a, r, cb, col0);
+  finish_item<KIND, T, SMOOTH>(a, r, cb, gm, gs, gsum, lp);
 }
 
 template <int KIND, typename T, int V, bool SMOOTH, int POLY, bool PF = false, int UV = 4, int MINB = 1>
@@ -188,6 +214,9 @@ __global__ void __launch_bounds__(256, MINB) rowstat_kernel(const StatArgs a) {
     const int64_t len = iv ? ((a.N - col0) < a.seg ? (a.N - col0) : a.seg) : 0;
     const T* xs = static_cast<const T*>(a.x) + r * a.ld + col0;
 
+    LabelPick lp{0, 0.f, false};
+    if constexpr (KIND == kXent)
+      if (t == 0 && iv) lp = pick_label<T>(a, r, cb, col0);
     float m = kNegInf, s = 0.f, sum = 0.f;
     int64_t done = 0;
     if constexpr (V > 1) {
@@ -246,7 +275,7 @@ __global__ void __launch_bounds__(256, MINB) rowstat_kernel(const StatArgs a) {
       buf ^= 1;
     }
 
-    if (t == 0 && iv) finish_item<KIND, T, SMOOTH>(a, r, cb, col0, gm, gs, gsum);
+    if (t == 0 && iv) finish_item<KIND, T, SMOOTH>(a, r, cb, gm, gs, gsum, lp);
   }
 }
 
