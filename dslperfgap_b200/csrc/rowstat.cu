@@ -326,6 +326,9 @@ __global__ void __launch_bounds__(fused_threads<SMOOTH>(), DSLPG_FUSED_CTAS) xen
   int buf = 0;
   for (int64_t r = blockIdx.x; r < a.M; r += gridDim.x) {
     const T* xr = static_cast<const T*>(a.x) + r * a.ld;
+    // every thread needs the label and dloss (pass 2); loaded now, their latency hides behind pass 1
+    const LabelPick lp = pick_label<T>(a, r, 0, 0);
+    const float dl_row = load_any(f.dloss, r * f.dloss_stride, f.dloss_dt);
     float m = kNegInf, s = 0.f, sum = 0.f;
     // pass 1 marks the row's lines evict-last so that pass 2 finds them in L2
     // (without the hint it read about 1.8x the logits from DRAM)
@@ -377,14 +380,12 @@ __global__ void __launch_bounds__(fused_threads<SMOOTH>(), DSLPG_FUSED_CTAS) xen
       gsum = group_reduce<SumOp>(sum, red[buf], nw, 0);
       buf ^= 1;
     }
-    if (t == 0) finish_item<kXent, T, SMOOTH>(a, r, 0, 0, gm, gs, gsum);
+    if (t == 0) finish_item<kXent, T, SMOOTH>(a, r, 0, gm, gs, gsum, lp);
     // the lse finish_item stored, formed the same way by every thread
     const float lse = (fabsf(gm) < kPosInf) ? (gm + log2f(gs)) * kLn2 : kNaN;
-    const int64_t label = a.label64 ? static_cast<const int64_t*>(a.labels)[r]
-                                    : static_cast<int64_t>(static_cast<const int32_t*>(a.labels)[r]);
-    const float dl = (label != a.ignored) ? load_any(f.dloss, r * f.dloss_stride, f.dloss_dt) : 0.f;
+    const float dl = (lp.label != a.ignored) ? dl_row : 0.f;
     const GradRow b =
-        grad_row_consts(dl, a.scale, lse, a.lse_sq, SMOOTH, a.smoothing, a.total_classes, label, a.class_start);
+        grad_row_consts(dl, a.scale, lse, a.lse_sq, SMOOTH, a.smoothing, a.total_classes, lp.label, a.class_start);
 #ifndef DSLPG_FUSED_PASS2_U
 #define DSLPG_FUSED_PASS2_U 4
 #endif
