@@ -649,7 +649,11 @@ cudaError_t dispatch_vec(StatArgs a, cudaStream_t st) {
   const bool few_long = a.M * a.nseg < sm_count() && item_bytes >= 128 * 1024;
   if (tma_ok && (path == DSLPG_PATH_CLUSTER || (path == DSLPG_PATH_AUTO && few_long)))
     return launch_cluster_stat<KIND, T, SMOOTH>(a, st);
-  if (vec && path != DSLPG_PATH_STREAM) return launch_stat<KIND, T, E, SMOOTH, 4, true, 4, 3>(a, st);
+  // With smoothing (the extra sum of the logits) the register bound of three
+  // CTAs spilled; two CTAs hold it in registers (vocab rows: 4982 against
+  // 4933 GB/s).
+  if (vec && path != DSLPG_PATH_STREAM)
+    return launch_stat<KIND, T, E, SMOOTH, 4, true, 4, (SMOOTH ? 2 : 3)>(a, st);
   return launch_stat<KIND, T, 1, SMOOTH>(a, st);
 }
 
