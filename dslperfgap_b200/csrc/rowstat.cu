@@ -217,6 +217,13 @@ __global__ void __launch_bounds__(256, MINB) rowstat_kernel(const StatArgs a) {
     LabelPick lp{0, 0.f, false};
     if constexpr (KIND == kXent)
       if (t == 0 && iv) lp = pick_label<T>(a, r, cb, col0);
+    // logsumexp: the same kind of row-start scalar read (the item's first
+    // element), consumed at the finish. Measured on B200, logsumexp bf16
+    // [8192,128256]: 0.903 -> 0.947 of the measured copy bandwidth, repeatable,
+    // at unchanged occupancy; why it helps (the compiled schedule differs) is
+    // not established.
+    if constexpr (KIND == kLse)
+      if (t == 0 && iv) lp.xl = to_f(static_cast<const T*>(a.x)[r * a.ld + col0]);
     float m = kNegInf, s = 0.f, sum = 0.f;
     int64_t done = 0;
     if constexpr (V > 1) {
@@ -275,6 +282,7 @@ __global__ void __launch_bounds__(256, MINB) rowstat_kernel(const StatArgs a) {
       buf ^= 1;
     }
 
+    if constexpr (KIND == kLse) asm volatile("" ::"f"(lp.xl));  // keeps the row-start read
     if (t == 0 && iv) finish_item<KIND, T, SMOOTH>(a, r, cb, gm, gs, gsum, lp);
   }
 }
