@@ -397,8 +397,8 @@ __global__ void __launch_bounds__(fused_threads<SMOOTH>(), DSLPG_FUSED_CTAS) xen
 #ifndef DSLPG_FUSED_PASS2_U
 #define DSLPG_FUSED_PASS2_U 4
 #endif
-    grad_row<T, V, false, DSLPG_FUSED_PASS2_U>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH,
-                                               t, kFusedThreads);
+    grad_row<T, V, DSLPG_FUSED_PASS2_U>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH, t,
+                                        kFusedThreads);
   }
 }
 

@@ -46,63 +46,76 @@ DSLPG_DEV float grad_elem(const GradRow& b, float x, float scale, bool is_label,
   return b.k1 * p;
 }
 
+// The per-row constants of the vector path, packed in f32x2 pairs.
+struct GradPairs {
+  f32x2 nl2, l2e2, fac2, nsn2, k12;
+};
+
+DSLPG_DEV GradPairs grad_pairs(const GradRow& b, float scale) {
+  GradPairs c;
+  c.nl2 = pk2(-b.lse * kLog2e, -b.lse * kLog2e);
+  c.l2e2 = pk2(kLog2e * scale, kLog2e * scale);
+  c.fac2 = pk2(b.fac, b.fac);
+  c.nsn2 = pk2(-b.sn, -b.sn);
+  c.k12 = pk2(b.k1, b.k1);
+  return c;
+}
+
+// The gradients of one 16-byte vector of logits, stored at dst.
+template <typename T>
+DSLPG_DEV void grad_vec(const Vec16& v, const GradPairs& c, bool smooth, T* dst) {
+  constexpr int P = Elt<T>::kPerVec / 2;
+  f32x2 y[P];
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    // exp(x * scale - lse) = 2^(x * scale * log2e - lse * log2e)
+    float d0, d1;
+    upk2(fma2(unpack_pair<T>(v, p), c.l2e2, c.nl2), d0, d1);
+    f32x2 e = pk2(ex2(d0), ex2(d1));
+    e = fma2(c.fac2, e, e);
+    if (smooth) e = add2(e, c.nsn2);
+    y[p] = mul2(c.k12, e);
+  }
+  StorePairs<T, P>::run(dst, y);
+}
+
+// The label column of a row, rewritten by the thread that wrote its vector
+// (V > 1) or element (V == 1), after that thread's own store.
+template <typename T, int V>
+DSLPG_DEV void grad_label_fix(const T* xr, T* yr, int64_t N, const GradRow& b, float scale, bool smooth, int t,
+                              int tpr) {
+  if (b.adj >= 0 && b.adj < N) {
+    const int64_t unit = (V > 1) ? b.adj / V : b.adj;
+    if (static_cast<int>(unit % tpr) == t) yr[b.adj] = from_f<T>(grad_elem(b, to_f(xr[b.adj]), scale, true, smooth));
+  }
+}
+
 // Write the N gradients of one row (xr -> yr) with the tpr threads t of a
-// group: 16-byte vectors (V > 1, nvec = N / V) or scalars (V == 1). The label
-// column is rewritten afterwards by the thread that wrote its vector, so it is
-// ordered after that thread's own vector store.
-// LAST_USE: the row's loads carry an L2 evict-first policy (its last read).
-// U: 16-byte loads in flight per thread.
-template <typename T, int V, bool LAST_USE = false, int U = 4>
+// group: 16-byte vectors (V > 1, nvec = N / V) or scalars (V == 1), then the
+// label column. U: 16-byte loads in flight per thread.
+template <typename T, int V, int U = 4>
 DSLPG_DEV void grad_row(const T* xr, T* yr, int nvec, int64_t N, const GradRow& b, float scale, bool smooth, int t,
                         int tpr) {
   if constexpr (V > 1) {
-    constexpr int P = V / 2;
-    const f32x2 nl2 = pk2(-b.lse * kLog2e, -b.lse * kLog2e);
-    const f32x2 l2e2 = pk2(kLog2e * scale, kLog2e * scale);
-    const f32x2 fac2 = pk2(b.fac, b.fac), nsn2 = pk2(-b.sn, -b.sn), k12 = pk2(b.k1, b.k1);
-    uint64_t pol = 0;
-    if constexpr (LAST_USE) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    const GradPairs c = grad_pairs(b, scale);
     for (int j0 = t; j0 < nvec; j0 += U * tpr) {
       Vec16 v[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int j = j0 + u * tpr;
         v[u] = Vec16{{0u, 0u, 0u, 0u}};
-        if (j < nvec) {
-          if constexpr (LAST_USE) {
-            asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
-                : "=r"(v[u].w[0]), "=r"(v[u].w[1]), "=r"(v[u].w[2]), "=r"(v[u].w[3])
-                : "l"(xr + static_cast<int64_t>(j) * V), "l"(pol));
-          } else {
-            v[u] = ld_stream(xr + static_cast<int64_t>(j) * V);
-          }
-        }
+        if (j < nvec) v[u] = ld_stream(xr + static_cast<int64_t>(j) * V);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int j = j0 + u * tpr;
-        if (j >= nvec) continue;
-        f32x2 y[P];
-#pragma unroll
-        for (int p = 0; p < P; ++p) {
-          // exp(x * scale - lse) = 2^(x * scale * log2e - lse * log2e)
-          float d0, d1;
-          upk2(fma2(unpack_pair<T>(v[u], p), l2e2, nl2), d0, d1);
-          f32x2 e = pk2(ex2(d0), ex2(d1));
-          e = fma2(fac2, e, e);
-          if (smooth) e = add2(e, nsn2);
-          y[p] = mul2(k12, e);
-        }
-        StorePairs<T, P>::run(yr + static_cast<int64_t>(j) * V, y);
+        if (j < nvec) grad_vec<T>(v[u], c, smooth, yr + static_cast<int64_t>(j) * V);
       }
     }
   } else {
     for (int64_t c = t; c < N; c += tpr) yr[c] = from_f<T>(grad_elem(b, to_f(xr[c]), scale, false, smooth));
   }
-  if (b.adj >= 0 && b.adj < N) {
-    const int64_t unit = (V > 1) ? b.adj / V : b.adj;
-    if (static_cast<int>(unit % tpr) == t) yr[b.adj] = from_f<T>(grad_elem(b, to_f(xr[b.adj]), scale, true, smooth));
-  }
+  grad_label_fix<T, V>(xr, yr, N, b, scale, smooth, t, tpr);
 }
 
 }  // namespace dslpg
