@@ -103,13 +103,17 @@ DSLPG_DEV uint64_t smem_desc_sw128(uint32_t saddr) {
 }
 
 // Instruction descriptor, kind::f16: fp32 accumulator, fp16 A and B, both
-// K-major, N = 128, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+// K-major, M = 128, N = 128 (one of w1 / w3) or 256 (w1 and w3 stacked).
+template <int N>
+constexpr uint32_t idesc_m128() {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
 
+template <int N>
 DSLPG_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+      "l"(adesc), "l"(bdesc), "r"(idesc_m128<N>()), "r"(accumulate));
 }
 
 DSLPG_DEV void umma_commit(uint32_t bar) {
@@ -281,11 +285,17 @@ __global__ void __launch_bounds__(kFfThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {  // K = 16 per MMA: 32 bytes into the swizzled rows
             const uint64_t ad = smem_desc_sw128(st + 32u * k);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+#ifdef DSLPG_FF1_TWO_MMAS
             const uint64_t b1 = smem_desc_sw128(st + kTileA + 32u * k);
             const uint64_t b3 = smem_desc_sw128(st + kTileA + kTileB + 32u * k);
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            umma_f16(acc_base, ad, b1, acc);
-            umma_f16(acc_base + kBN, ad, b3, acc);
+            umma_f16<kBN>(acc_base, ad, b1, acc);
+            umma_f16<kBN>(acc_base + kBN, ad, b3, acc);
+#else
+            // the w1 tile and the w3 tile lie back to back (128 rows each, 1024-byte
+            // row groups), one 256-row operand: TMEM columns 0-127 get acc1, 128-255 acc3
+            umma_f16<2 * kBN>(acc_base, ad, smem_desc_sw128(st + kTileA + 32u * k), acc);
+#endif
           }
           umma_commit(empty0 + 8u * s);  // the stage is free once these MMAs have read it
         }
