@@ -65,6 +65,20 @@ __global__ void __launch_bounds__(256, MINB) reduce_rows_kernel(const RedArgs a)
   const int nw = a.tpr >> 5, first_warp = g * nw, lane = threadIdx.x & 31;
   const int64_t step = static_cast<int64_t>(gridDim.x) * a.rpc;
 
+  // the first chunk of a row's loads (U vectors per thread)
+  Vec16 nx[V > 1 ? U : 1];
+  auto first_chunk = [&](int64_t row) {
+    if constexpr (V > 1) {
+      const Tin* xr = static_cast<const Tin*>(a.x) + row * a.N;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t j = t + static_cast<int64_t>(u) * a.tpr;
+        nx[u] = Vec16{{0u, 0u, 0u, 0u}};
+        if (row < a.M && j < a.nvec) nx[u] = ld_stream(xr + j * V);
+      }
+    }
+  };
+  first_chunk(static_cast<int64_t>(blockIdx.x) * a.rpc + g);
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * a.rpc; base < a.M; base += step) {
     const int64_t row = base + g;
     const bool rv = row < a.M;
@@ -74,15 +88,7 @@ __global__ void __launch_bounds__(256, MINB) reduce_rows_kernel(const RedArgs a)
     int64_t best_j = -1;  // vector path: the vector holding best.v, and its data
     Vec16 best_vec{{0u, 0u, 0u, 0u}};
     const int64_t units = rv ? ((V > 1) ? a.nvec : a.N) : 0;
-    Vec16 nx[V > 1 ? U : 1];
-    if constexpr (V > 1) {
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t j = t + static_cast<int64_t>(u) * a.tpr;
-        nx[u] = Vec16{{0u, 0u, 0u, 0u}};
-        if (j < units) nx[u] = ld_stream(xr + j * V);
-      }
-    }
+
     for (int64_t j0 = t; j0 < units; j0 += static_cast<int64_t>(U) * a.tpr) {
       if constexpr (V > 1) {
         constexpr int P = V / 2;
@@ -146,6 +152,9 @@ __global__ void __launch_bounds__(256, MINB) reduce_rows_kernel(const RedArgs a)
       }
     }
 
+    // The next row's first loads fly during this row's merge (max / argmax:
+    // 0.830 -> 0.845 of measured HBM; it costs max / argmax a 4-byte spill).
+    first_chunk(row + step);
     if constexpr (OP != kMean && V > 1) {
       if (best_j >= 0) {  // first position of the maximum (or first NaN) in its vector
         float f[V];
