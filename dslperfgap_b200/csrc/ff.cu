@@ -11,6 +11,8 @@
 //  * ff_prologue_kernel: one pass over x per row (a warp per row): a_norm and xs.
 //  * ff_gemm2_kernel (M > 128): CTA pairs on 256x128 tiles with
 //    tcgen05.mma.cta_group::2 — described where it is defined;
+//  * ff_gemv_kernel (M <= 3 by default): one warp per output column streaming
+//    the weight rows, for decode-like shapes — described where it is defined;
 //  * ff_gemm_kernel (M <= 128): persistent, one CTA per SM walking 128x128 output tiles,
 //    warp-specialised:
 //      warp 0 (one lane)  TMA tensor loads of xs / w1 / w3 tiles (BK = 64,
@@ -627,6 +629,100 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFfThreads, 1)
   }
 }
 
+// ---------------------------------------------------------- few rows (GEMV)
+// ff_gemv_kernel: M <= 3 by default (decode-like). Reading the weights is the
+// whole cost, and the tensor-core kernels read each weight row in 128-byte
+// pieces, 256 rows at a time. Here one warp takes one output column n at a
+// time and streams the weight rows w1[n] and w3[n] contiguously (512 bytes per
+// warp load, U loads of each in flight), against the M rows of xs staged in
+// shared memory; fp32 accumulation on f32x2 pairs, a warp butterfly, and lane
+// m applies the a_norm scale and the SiLU gate of row m.
+constexpr int kGemvMaxRows = 8;   // the kernel's limit (DSLPG_PATH_STREAM forces it up to here)
+constexpr int kGemvAutoRows = 3;  // chosen by default up to here. Measured per call (K = 4096,
+                                  // N = 16384) against the tensor-core kernel: 50.7 / 68.0 us at M = 1,
+                                  // 52.9 / 68.7 at M = 2, 65.8 / 68.4 at M = 3, even at M = 4, 117 / 72
+                                  // at M = 8 (its CUDA-core FMAs grow with M)
+constexpr int kGemvThreads = 256;
+constexpr int kGemvMaxSmem = 96 * 1024;  // xs staged per CTA: M * K * 2 bytes at most
+
+template <int MB>
+__global__ void __launch_bounds__(kGemvThreads) ff_gemv_kernel(const __half* __restrict__ xs,
+                                                               const __half* __restrict__ w1,
+                                                               const __half* __restrict__ w3, const FfArgs a) {
+  constexpr int U = 4;
+  extern __shared__ __align__(16) unsigned char smem_g[];
+  const int K = a.K, M = static_cast<int>(a.M), kv = K / 8;
+  Vec16* sx = reinterpret_cast<Vec16*>(smem_g);  // [M][kv]
+  for (int i = threadIdx.x; i < M * kv; i += kGemvThreads) sx[i] = ld_keep(xs + static_cast<int64_t>(i) * 8);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kGemvThreads / 32);
+  for (int64_t n = static_cast<int64_t>(blockIdx.x) * (kGemvThreads / 32) + (threadIdx.x >> 5); n < a.N;
+       n += nwarps) {
+    const __half* r1 = w1 + n * K;
+    const __half* r3 = w3 + n * K;
+    f32x2 acc1[MB], acc3[MB];
+#pragma unroll
+    for (int m = 0; m < MB; ++m) acc1[m] = acc3[m] = pk2(0.f, 0.f);
+    for (int j0 = lane; j0 < kv; j0 += 32 * U) {
+      Vec16 v1[U], v3[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + 32 * u;
+        if (j < kv) {
+          v1[u] = ld_stream(r1 + static_cast<int64_t>(j) * 8);
+          v3[u] = ld_stream(r3 + static_cast<int64_t>(j) * 8);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + 32 * u;
+        if (j >= kv) continue;
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+          if (m >= M) break;
+          const Vec16 xv = sx[m * kv + j];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const f32x2 xp = unpack_pair<__half>(xv, p);
+            acc1[m] = fma2(unpack_pair<__half>(v1[u], p), xp, acc1[m]);
+            acc3[m] = fma2(unpack_pair<__half>(v3[u], p), xp, acc3[m]);
+          }
+        }
+      }
+    }
+    float mine1 = 0.f, mine3 = 0.f;
+#pragma unroll
+    for (int m = 0; m < MB; ++m) {
+      if (m >= M) break;
+      const float s1 = warp_reduce<SumOp>(hsum2(acc1[m]));
+      const float s3 = warp_reduce<SumOp>(hsum2(acc3[m]));
+      if (lane == m) {
+        mine1 = s1;
+        mine3 = s3;
+      }
+    }
+    if (lane < M) {
+      const float an = a.a_norm[lane];
+      const float g = mine1 * an, u = mine3 * an;
+      const float sig = rcp_approx(1.0f + ex2(-g * kLog2e));
+      a.out[static_cast<int64_t>(lane) * a.N + n] = __float2half_rn((g * sig) * u);
+    }
+  }
+}
+
+namespace {
+template <int MB>
+cudaError_t launch_gemv(const __half* xs, const __half* w1, const __half* w3, const FfArgs& args, cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&ff_gemv_kernel<MB>);
+  const size_t smem = static_cast<size_t>(args.M) * args.K * 2;
+  if (cudaError_t e = allow_dynamic_smem(fn, smem)) return e;
+  const int grid = persistent_grid(fn, kGemvThreads, smem, (args.N + 7) / 8);
+  ff_gemv_kernel<MB><<<grid, kGemvThreads, smem, st>>>(xs, w1, w3, args);
+  return cudaGetLastError();
+}
+}  // namespace
+
 // ------------------------------------------------------------------- host
 namespace {
 
@@ -704,6 +800,18 @@ extern "C" int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, co
 
   FfArgs args{a_norm, static_cast<__half*>(out), M, N, static_cast<int>(K)};
   const int path = kernel_path();
+  // Few rows: the weight-streaming kernel (DSLPG_PATH_STREAM forces it where it applies).
+  const bool gemv_fits = M <= kGemvMaxRows && M * K * 2 <= kGemvMaxSmem;
+  if (gemv_fits && ((path == DSLPG_PATH_AUTO && M <= kGemvAutoRows) || path == DSLPG_PATH_STREAM)) {
+    const __half* w1h = static_cast<const __half*>(w1);
+    const __half* w3h = static_cast<const __half*>(w3);
+    cudaError_t e;
+    if (M == 1) e = launch_gemv<1>(xs, w1h, w3h, args, stream);
+    else if (M == 2) e = launch_gemv<2>(xs, w1h, w3h, args, stream);
+    else if (M <= 4) e = launch_gemv<4>(xs, w1h, w3h, args, stream);
+    else e = launch_gemv<8>(xs, w1h, w3h, args, stream);
+    return static_cast<int>(e);
+  }
   const bool use_pair = path == DSLPG_PATH_CLUSTER || (path != DSLPG_PATH_RESIDENT && M > kBM);
   CUtensorMap ma, mb1, mb3;
   if (!make_map(&ma, xs, M, static_cast<int>(K)) || !make_map(&mb1, w1, N, static_cast<int>(K)) ||

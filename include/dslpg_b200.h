@@ -63,7 +63,8 @@ enum {
   DSLPG_PATH_AUTO = 0,     /* pick per shape */
   DSLPG_PATH_RESIDENT = 1, /* rows read straight into registers; kernel_ff: one CTA per 128x128 tile */
   DSLPG_PATH_TMA = 2,      /* rows / row chunks staged by TMA bulk copies */
-  DSLPG_PATH_STREAM = 3,   /* two-pass streaming (any length or alignment) */
+  DSLPG_PATH_STREAM = 3,   /* two-pass streaming (any length or alignment); kernel_ff: the weight-streaming
+                              kernel for M <= 8 (chosen by default for M <= 3) */
   DSLPG_PATH_CLUSTER = 4   /* a row split over a thread-block cluster (DSMEM exchange);
                               kernel_ff: CTA pairs (tcgen05 cta_group::2) on 256x128 tiles */
 };

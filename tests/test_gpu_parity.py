@@ -408,11 +408,15 @@ def test_cross_entropy_few_long_rows(bs, smooth):
 
 
 # ------------------------------------------------ linear_activation.kernel_ff
-# path: "auto" (one CTA per tile for M <= 128, CTA pairs above), "resident"
-# (force one CTA per 128x128 tile), "cluster" (force CTA pairs on 256x128 tiles)
-@pytest.mark.parametrize("path", ["auto", "resident", "cluster"])
+# path: "auto" (the weight-streaming kernel for M <= 3, one CTA per tile up to
+# M = 128, CTA pairs above), "stream" (force the weight-streaming kernel for
+# M <= 8), "resident" (force one CTA per 128x128 tile), "cluster" (force CTA
+# pairs on 256x128 tiles)
+@pytest.mark.parametrize("path", ["auto", "stream", "resident", "cluster"])
 @pytest.mark.parametrize("b,s,d,n", [(1, 128, 64, 128), (1, 128, 128, 256), (2, 100, 512, 200), (1, 256, 1024, 512),
-                                     (1, 300, 2048, 640), (3, 7, 72, 40), (1, 1000, 320, 1000), (4, 700, 256, 2176)])
+                                     (1, 300, 2048, 640), (3, 7, 72, 40), (1, 1000, 320, 1000), (4, 700, 256, 2176),
+                                     (1, 1, 64, 128), (1, 1, 4096, 1000), (1, 2, 1032, 300), (1, 3, 256, 129),
+                                     (2, 2, 4096, 2048), (1, 5, 520, 77), (1, 8, 4096, 4096), (8, 1, 6144, 512)])
 def test_kernel_ff(b, s, d, n, path):
     g = gen(d + n)
     x = randn((b, s, d), torch.float16, g)
