@@ -239,7 +239,8 @@ DSLPG_API int dslpg_rms_norm_fwd_host(const void* x_host, const void* weight, vo
                                       cudaStream_t stream);
 
 /*
- * Llama feed-forward with the RMSNorm fused around a tensor-core dual GEMM:
+ * Llama feed-forward with the RMSNorm fused around a dual GEMM (tcgen05 tensor
+ * cores; for M <= 3 rows a kernel that streams the weight rows instead):
  *   a_norm[m] = rsqrt(sum_k x[m,k]^2 / K + 1e-6);  xs = x * rms_w (fp16);
  *   out[m,n] = silu(a_norm[m] * (xs @ w1^T)[m,n]) * (a_norm[m] * (xs @ w3^T)[m,n])   (fp16)
  * x [M, K], w1 and w3 [N, K], rms_w [K], out [M, N]: all fp16, row-major,
