@@ -8,24 +8,30 @@ Metric: achieved HBM GB/s (algorithmic bytes: inputs read once + outputs
 written once) per kernel, as a fraction of the measured B200 copy bandwidth,
 with E_lib = t_torch / t_cuda * 100 against the torch GPU operator.
 
-A step is one launch of the op over one batch of a workload. The headline
-workload is the RMSNorm bf16 [16384, 8192] configuration; every other
-configuration is timed too and reported under "kernels". Under torchrun each
-rank runs on its own GPU: the headline and the single-GPU workloads are
-replicated per rank (weak scaling), the row-sharded LayerNorm is split into
-row blocks (strong scaling); there is no collective on the data path (NCCL
-only carries the max-over-ranks of the timings).
+Headline (every N): the row-sharded LayerNorm bf16 x[131072, 8192], 2 GiB in
+and 2 GiB out, split into contiguous row blocks over the N ranks (strong
+scaling: the total work is fixed). A step is one launch of the kernel over
+each rank's row block. The K timed steps run back to back between a barrier +
+device synchronise on both sides; each rank's region is one CUDA-event pair
+on the launching stream, and the reported time is the max over ranks (the
+common start to the last rank done). L2: each rank's block is at least
+256 MiB, larger than the 126 MB L2, and two copies of it alternate between
+steps, so no step reads a line the step before touched. `value` is the whole
+job's algorithmic bytes over that time. `e2e` is the same step through the
+public host-buffer API (`layer_norm_host`: pinned host rows in, host rows
+out, copies inside the timed region).
 
-Timing: W untimed warm-up steps, then exactly K steps; before each step a
-512 MiB buffer is written (L2 flush, and it keeps the GPU busy while the host
-enqueues the step); each step is bracketed by CUDA events on the launching
-stream. The K-step region is bracketed by a barrier and device synchronise;
-the reported time is the max over ranks. SM clocks and throttle reasons are
-sampled (NVML, read-only) during the timed regions.
+At N = 1 every other configuration is timed too (under "kernels"), each step
+after a 512 MiB L2-flush write and bracketed by its own CUDA events, beside its
+torch GPU operator; the reference's own benchmark shapes run with its own
+protocol ("reference_shapes"). SM clocks and throttle reasons are sampled
+(NVML, read-only) during the timed regions.
 
---impl reference times the CPU implementation of the same path (the oracle
-restatement of the reference's pytorch_impl, all host threads) on a bounded
-sample of the same workload; under torchrun only rank 0 runs it.
+--impl reference times the reference's CPU path for the same workload and
+metric: the torch CPU operators of ViperBench/<kernel>/pytorch_impl.py
+(restated in oracle/torch_cpu.py, since the checkout is not on the GPU box)
+on all host threads, over the whole configuration; under torchrun only rank 0
+runs it.
 """
 from __future__ import annotations
 
@@ -47,7 +53,7 @@ sys.path.insert(0, str(ROOT))
 from dslperfgap_b200 import workloads  # noqa: E402
 
 METRIC = "HBM GB/s and % of B200 peak per kernel at 1/2/4/8 GPUs; E_lib vs torch"
-HEADLINE = "rms_norm_bf16"
+HEADLINE = "layer_norm_bf16_sharded"
 SPEC_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 FLUSH_BYTES = 512 << 20
@@ -225,6 +231,39 @@ class Timer:
             sampler.active = False
         self.barrier()
         return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+    def time_region(self, fn, steps, warmup, sampler=None):
+        """Run fn(k) for k in 0..warmup-1 untimed, then fn(k) for k in 0..steps-1
+        back to back between a barrier + device synchronise on both sides.
+        Returns (per-step device ms of this rank, this rank's region ms): one
+        event before each step and one after the last, all on the launching
+        stream, so the region is the first step's start to the last step's end."""
+        for k in range(warmup):
+            fn(k)
+        torch.cuda.synchronize(self.device)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        self.barrier()
+        if sampler:
+            sampler.active = True
+        for k in range(steps):
+            ev[k].record()
+            fn(k)
+        ev[steps].record()
+        torch.cuda.synchronize(self.device)
+        if sampler:
+            sampler.active = False
+        self.barrier()
+        per = [ev[k].elapsed_time(ev[k + 1]) for k in range(steps)]
+        return per, ev[0].elapsed_time(ev[steps])
+
+    def gather(self, value: float) -> list:
+        """value from every rank, in rank order."""
+        if self.world == 1:
+            return [value]
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        torch.distributed.all_gather(out, t)
+        return [float(o.item()) for o in out]
 
     def max_over_ranks(self, value: float) -> float:
         if self.world == 1:
@@ -493,6 +532,90 @@ def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler
     return res
 
 
+def measure_sharded(name, rank, world, dev, timer, steps, warmup, peak, sampler, with_torch=True):
+    """The strong-scaled headline: rank r normalises its row block of `name`
+    (workloads.shard_rows); K launches back to back, alternating between two
+    copies of the block (each larger than L2), timed as one region per rank;
+    the job's time is the max over ranks."""
+    cfg = workloads.CONFIGS[name]
+    rows = workloads.shard_rows(cfg.M, rank, world)
+    if ROWS_OVERRIDE:  # a small slice, for profiling captures
+        rows = (rows[0], min(rows[1], rows[0] + ROWS_OVERRIDE))
+    wl = workloads.make(name, seed=0, device=dev, rows=rows)
+    launch = direct_launcher(wl, dev)
+    x0 = wl.args[0]
+    blocks = [x0, x0.clone()]
+
+    def step(k):
+        wl.args[0] = blocks[k % 2]
+        launch()
+
+    per, region = timer.time_region(step, steps, warmup, sampler)
+    wl.args[0] = x0
+    regions = timer.gather(region)
+    t_max = max(regions)
+    bytes_rank = wl.algo_bytes()
+    total_bytes = bytes_rank * world * steps if ROWS_OVERRIDE else workloads.algo_bytes(cfg, cfg.M) * steps
+    kernel_ms = statistics.mean(per)
+    achieved = bytes_rank / (kernel_ms * 1e-3) / 1e9
+    res = {
+        "shape": [cfg.M, cfg.N], "dtype": SHORT[cfg.dtype], "rows_per_gpu": wl.M, "scaling": "strong",
+        "ms_per_step": round(t_max / steps, 5), "median_ms": round(statistics.median(per), 5),
+        "gbs": round(total_bytes / (t_max * 1e-3) / 1e9, 1), "gbs_per_gpu": round(achieved, 1),
+        "frac_measured": round(achieved / peak, 4), "frac_spec": round(achieved / SPEC_HBM_GBS, 4),
+        "algo_bytes_per_launch": bytes_rank,
+        "region_ms_per_rank": [round(r, 4) for r in regions],
+        "straggler_spread_pct": round(100.0 * (max(regions) - min(regions)) / max(regions), 2),
+        "timing": "one CUDA-event region per rank over the K steps (barrier + synchronise on both sides), "
+                  "max over ranks",
+        "launches": steps,
+    }
+    if with_torch:
+        import torch.nn.functional as F
+        w, b = wl.args[1], wl.args[2]
+        tp, treg = timer.time_region(lambda k: F.layer_norm(blocks[k % 2], (cfg.N,), w, b, 1e-5), steps, warmup)
+        t_torch = max(timer.gather(treg)) / steps
+        res["torch_op"] = "F.layer_norm"
+        res["torch_ms"] = round(t_torch, 5)
+        res["e_lib_pct"] = round(100.0 * t_torch / res["ms_per_step"], 1)
+    del launch, blocks
+    return res, wl
+
+
+def measure_e2e_sharded(wl, world, dev, timer, steps, warmup):
+    """`value`'s metric through the public API with host buffers: each rank
+    passes its row block in pinned host memory to dslperfgap_b200.layer_norm_host
+    (dslpg_layer_norm_fwd_host: 16 MiB chunks uploaded, normalised and
+    downloaded with both copy directions overlapped) and gets the rows back in
+    pinned host memory; the copies are inside the timed region. Max over ranks."""
+    import dslperfgap_b200 as B
+    cfg = wl.config
+    x_dev, w, b = wl.args
+    x_host = torch.empty(x_dev.shape, dtype=x_dev.dtype, pin_memory=True)
+    x_host.copy_(x_dev)
+    y_host = torch.empty_like(x_host).pin_memory()
+
+    def step(k):
+        B.layer_norm_host(x_host, w, b, out=y_host)
+
+    per, region = timer.time_region(step, steps, warmup)
+    t_max = max(timer.gather(region))
+    total = workloads.algo_bytes(cfg, cfg.M) * steps
+    y_dev = B.layer_norm(x_dev, w, b)
+    ok = bool(torch.equal(y_host.to(dev), y_dev))
+    chunk_rows = max(1, (16 << 20) // (cfg.N * x_host.element_size()))
+    del y_dev
+    return {"value": round(total / (t_max * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+            "d2h_bytes_per_step": y_host.numel() * y_host.element_size(),
+            "bytes_note": "per rank; the job moves world x these",
+            "ms_per_step": round(t_max / steps, 4),
+            "path": "dslperfgap_b200.layer_norm_host (public API) -> dslpg_layer_norm_fwd_host, pinned host buffers, "
+                    "16 MiB chunks with uploads, kernels and downloads overlapped; each rank its own row block",
+            "result_matches_device_path": ok,
+            "launches": steps * -(-wl.M // chunk_rows)}
+
+
 def measure_e2e(name, rank, world, dev, timer, steps, warmup):
     """Same metric through the public API with pinned host buffers:
     dslperfgap_b200.rms_norm_host takes the step's input in host memory and
@@ -647,46 +770,69 @@ def reference_shapes(dev):
 
 
 # ----------------------------------------------------------------- CPU baseline
-def cpu_sample(name, target_s=1.0):
-    """Time the oracle (all host threads) on a bounded row sample; returns dict."""
-    from oracle import oracle
-    cfg = workloads.CONFIGS[name]
-    fn = getattr(oracle, cfg.fn_name)
-    rows = max(1, min(cfg.M, (1 << 20) // cfg.N))
-    wl = workloads.make(name, seed=0, device="cpu", rows=(0, rows))
-    t0 = time.perf_counter()
-    fn(*wl.args, **wl.kwargs)
-    dt = time.perf_counter() - t0
-    rows = max(1, min(cfg.M, int(rows * target_s / max(dt, 1e-6))))
-    wl = workloads.make(name, seed=0, device="cpu", rows=(0, rows))
-    return wl, fn
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
 
-def run_cpu_baseline(name, seconds=10.0):
-    from oracle import oracle
-    wl, fn = cpu_sample(name, target_s=seconds / 5)
-    fn(*wl.args, **wl.kwargs)  # warm
+def _cpu_impls(cfg):
+    """(label, kind, function, threads) of the CPU implementations of `cfg`'s op:
+    the torch CPU operators of the reference's pytorch_impl (oracle/torch_cpu.py)
+    where that file restates the op, and the C restatement (oracle/oracle.c)."""
+    from oracle import oracle, torch_cpu
+    out = []
+    if cfg.fn_name in torch_cpu.FUNCTIONS:
+        out.append((f"torch CPU operators of ViperBench/{cfg.op}/pytorch_impl.py (oracle/torch_cpu.py)", "port",
+                    torch_cpu.FUNCTIONS[cfg.fn_name], torch_cpu.threads))
+    out.append((f"C restatement of ViperBench/{cfg.op}/pytorch_impl.py (oracle/oracle.c), fp64 accumulation",
+                "port", getattr(oracle, cfg.fn_name), oracle.threads))
+    return out
+
+
+def _time_cpu(fn, wl, reps):
+    fn(*wl.args, **wl.kwargs)  # warm (page-in, thread pools)
     times = []
-    for _ in range(5):
+    for _ in range(reps):
         t0 = time.perf_counter()
         fn(*wl.args, **wl.kwargs)
         times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    gbs = wl.algo_bytes() / t / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": oracle.threads(), "kind": "port",
-            "sample": f"{wl.M} of {wl.config.M} rows of {name} ({wl.algo_bytes()} algorithmic bytes), median of 5 "
-                      f"calls of the C oracle (restatement of ViperBench/{wl.config.op}/pytorch_impl.py), "
-                      f"{oracle.threads()} host threads"}
+    return times
+
+
+def run_cpu_baseline(name, seconds=10.0):
+    """Each CPU implementation on a bounded row sample of `name` (about
+    `seconds` of work each), on every host thread."""
+    torch.set_num_threads(host_threads())
+    cfg = workloads.CONFIGS[name]
+    results = []
+    for label, kind, fn, nthreads in _cpu_impls(cfg):
+        probe_rows = max(1, min(cfg.M, (8 << 20) // cfg.N))
+        wl = workloads.make(name, seed=0, device="cpu", rows=(0, probe_rows))
+        dt = statistics.median(_time_cpu(fn, wl, 1))
+        rows = max(1, min(cfg.M, int(probe_rows * (seconds / 5) / max(dt, 1e-6))))
+        wl = workloads.make(name, seed=0, device="cpu", rows=(0, rows))
+        t = statistics.median(_time_cpu(fn, wl, 5))
+        results.append({"value": round(wl.algo_bytes() / t / 1e9, 3), "unit": "GB/s", "cores": nthreads(),
+                        "kind": kind, "host_cpus": os.cpu_count(),
+                        "sample": f"{wl.M} of {cfg.M} rows of {name} ({wl.algo_bytes()} algorithmic bytes), median of "
+                                  f"5 calls; {label}, {nthreads()} host threads"})
+    best = dict(results[0])
+    best["others"] = results[1:]
+    return best
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the CPU implementation of the path on the host cores."""
+    """--impl reference: the reference's CPU path (the torch CPU operators of its
+    pytorch_impl) on the whole configuration, all host threads, rank 0 only."""
     if rank != 0:
         return 0
-    from oracle import oracle
+    torch.set_num_threads(host_threads())
     name = args.workload
     cfg = workloads.CONFIGS[name]
-    wl, fn = cpu_sample(name, target_s=0.25)
+    label, kind, fn, nthreads = _cpu_impls(cfg)[0]
+    wl = workloads.make(name, seed=0, device="cpu")
     for _ in range(args.warmup):
         fn(*wl.args, **wl.kwargs)
     times = []
@@ -696,18 +842,25 @@ def run_reference(args, rank, world):
         times.append(time.perf_counter() - t0)
     total = sum(times)
     gbs = wl.algo_bytes() * args.steps / total / 1e9
-    sample = (f"{wl.M} of {cfg.M} rows of {name} per step; C oracle restating "
-              f"ViperBench/{cfg.op}/pytorch_impl.py, {oracle.threads()} host threads")
+    sample = (f"all {cfg.M} rows of {name} every step ({wl.algo_bytes()} algorithmic bytes); {label}; "
+              f"{nthreads()} host threads of {os.cpu_count()} CPUs")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": SHORT[cfg.dtype],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": SHORT[cfg.dtype],
         "data": "synthetic (seeded, BASELINE distributions)",
         "config": workloads.config_dict(cfg),
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": oracle.threads(), "kind": "port",
+        "same_config": True,
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nthreads(), "kind": kind,
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_cpu_baseline:
+        # the C restatement on the same full configuration, for comparison
+        c_label, _, c_fn, c_threads = _cpu_impls(cfg)[-1]
+        ct = _time_cpu(c_fn, wl, max(1, min(3, args.steps)))
+        line["c_restatement"] = {"value": round(wl.algo_bytes() / statistics.median(ct) / 1e9, 3), "unit": "GB/s",
+                                 "cores": c_threads(), "sample": f"all {cfg.M} rows, median of {len(ct)}; {c_label}"}
     emit(line)
     return 0
 
@@ -759,17 +912,28 @@ def main(argv=None):
     sampler.start()
 
     with_torch = not args.kernel_only
-    head = measure_workload(args.workload, rank, world, dev, timer, args.steps, args.warmup, peak, sampler,
-                            with_torch)
+    sharded = args.workload == HEADLINE
+    e2e = None
+    if sharded:
+        head, head_wl = measure_sharded(args.workload, rank, world, dev, timer, args.steps, args.warmup, peak, sampler,
+                                        with_torch)
+        if not args.kernel_only:
+            e2e_steps = max(3, min(args.steps, 10))
+            e2e = measure_e2e_sharded(head_wl, world, dev, timer, e2e_steps, args.warmup)
+        del head_wl
+        torch.cuda.empty_cache()
+    else:
+        head = measure_workload(args.workload, rank, world, dev, timer, args.steps, args.warmup, peak, sampler,
+                                with_torch)
     kernels = {args.workload: head}
-    if not args.headline_only:
+    # The other configurations are single-GPU workloads: measured at N = 1 only.
+    if world == 1 and not args.headline_only:
         for name in workloads.NAMES:
             if name != args.workload:
                 kernels[name] = measure_workload(name, rank, world, dev, timer, args.steps, args.warmup, peak,
                                                  sampler, with_torch)
-    e2e_steps = max(3, min(args.steps, 20))
-    e2e = measure_e2e(HEADLINE, rank, world, dev, timer, e2e_steps, args.warmup) \
-        if args.workload == HEADLINE and not args.kernel_only else None
+    if world == 1 and not sharded and not args.kernel_only and args.workload == "rms_norm_bf16":
+        e2e = measure_e2e("rms_norm_bf16", rank, world, dev, timer, max(3, min(args.steps, 20)), args.warmup)
     sampler.stop()
     clocks = sampler.summary()
 
@@ -786,16 +950,27 @@ def main(argv=None):
     if rank == 0:
         cfg = workloads.CONFIGS[args.workload]
         traffic = profile_traffic().get(args.workload)
+        if sharded:
+            l2 = ("inputs larger than L2: each rank's row block is >= 256 MiB and two copies of it alternate "
+                  "between steps (no flush)")
+        else:
+            l2 = "512 MiB buffer written between timed steps"
         line = {
             "metric": METRIC, "value": head["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
             "scaling": head["scaling"], "vs_baseline": None, "dtype": SHORT[cfg.dtype],
             "data": "synthetic (seeded generators with the BASELINE shapes and distributions)",
-            "config": {**workloads.config_dict(cfg), "l2": "512 MiB buffer written between timed steps",
-                       "parallelism": f"row-independent; {world} rank(s), one per GPU, no data-path collective"},
+            "config": {**workloads.config_dict(cfg), "l2": l2,
+                       "parallelism": (f"row blocks of {cfg.M // world} rows on each of {world} GPU(s), one rank per "
+                                       "GPU, no data-path collective" if sharded else
+                                       f"replicated on {world} rank(s), one per GPU, no data-path collective")},
             "roofline": {"bound": "hbm", "achieved": head["gbs_per_gpu"], "peak": peak, "unit": "GB/s",
                          "frac": round(head["gbs_per_gpu"] / peak, 4),
                          "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                         "traffic_source": ("profiles/traffic.json: ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                            f"of {traffic.get('kernel')}, from a committed capture "
+                                            f"({traffic.get('note', 'full workload')}); not measured in this run")
+                         if traffic else None,
                          "peak_source": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
                          if peak_kind == "measured" else "fallback 6.65 TB/s"},
             "cpu_baseline": cpu,

@@ -52,6 +52,8 @@ SIGNATURES = {
     "dslpg_kernel_ff": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _c_i64, _vp],
     "dslpg_rms_norm_fwd_host_workspace_bytes": [_c_i64, _c_i64, _c_int, _vp],
     "dslpg_rms_norm_fwd_host": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_f32, _vp, _c_i64, _vp],
+    "dslpg_layer_norm_fwd_host_workspace_bytes": [_c_i64, _c_i64, _c_int, _vp],
+    "dslpg_layer_norm_fwd_host": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_f32, _vp, _c_i64, _vp],
     "dslpg_kernel_ff_static": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp],
     "dslpg_version": [],
     "dslpg_set_kernel_path": [_c_int],
@@ -185,6 +187,25 @@ class kernel_path:
     def __exit__(self, *exc):
         load().dslpg_set_kernel_path(0)
         return False
+
+
+def run_host_pipeline(name: str, x, out, dev: torch.device, m: int, n: int, xc: int, ptrs_before: tuple,
+                      ptrs_after: tuple) -> None:
+    """Shared tail of the host-buffer entry points (``dslpg_<op>_fwd_host``):
+    query the chunk workspace, allocate it on `dev` with torch's caching
+    allocator, launch `name`(x, *ptrs_before, out, m, n, xc, *ptrs_after,
+    workspace, bytes, stream) on `dev`'s current stream and wait for that
+    stream, so `out` is ready to read when this returns."""
+    lib = load()
+    need = ctypes.c_int64(0)
+    check(getattr(lib, name + "_workspace_bytes")(m, n, xc, ctypes.byref(need)), name + "_workspace_bytes")
+    with torch.cuda.device(dev):
+        ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        rc = getattr(lib, name)(x.data_ptr(), *ptrs_before, out.data_ptr(), m, n, xc, *ptrs_after, ws.data_ptr(),
+                                need.value, stream.cuda_stream)
+        check(rc, name)
+        stream.synchronize()
 
 
 def take_wait_timeouts() -> int:

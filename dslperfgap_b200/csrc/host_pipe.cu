@@ -1,4 +1,4 @@
-// host_pipe.cu — row ops on HOST buffers: the rows stream through the GPU in
+// host_pipe.cu — row ops (RMSNorm, LayerNorm) on HOST buffers: the rows stream through the GPU in
 // chunks, with the upload of chunk i+1, the kernel on chunk i and the download
 // of chunk i-1 in flight together (PCIe is full duplex, so with pinned host
 // memory the two copy directions overlap).
@@ -142,5 +142,25 @@ extern "C" int dslpg_rms_norm_fwd_host(const void* x_host, const void* weight, v
   return host_rows_pipeline(x_host, y_host, M, rb, rb, workspace, workspace_bytes, stream,
                             [&](void* in, void* out, int64_t rows, cudaStream_t st) {
                               return dslpg_rms_norm_fwd(in, weight, out, rows, N, x_dtype, w_dtype, eps, st);
+                            });
+}
+
+extern "C" int dslpg_layer_norm_fwd_host_workspace_bytes(int64_t M, int64_t N, int x_dtype, int64_t* bytes) {
+  return dslpg_rms_norm_fwd_host_workspace_bytes(M, N, x_dtype, bytes);
+}
+
+extern "C" int dslpg_layer_norm_fwd_host(const void* x_host, const void* weight, const void* bias, void* y_host,
+                                         int64_t M, int64_t N, int x_dtype, int w_dtype, float eps, void* workspace,
+                                         int64_t workspace_bytes, cudaStream_t stream) {
+  if (!x_host || !weight || !y_host) return DSLPG_ERR_NULL_POINTER;
+  if (M < 0 || N < 0) return DSLPG_ERR_BAD_SHAPE;
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(w_dtype)) return DSLPG_ERR_BAD_DTYPE;
+  if (!(eps >= 0.f) || !(eps < kPosInf)) return DSLPG_ERR_BAD_EPS;
+  if (M == 0 || N == 0) return DSLPG_OK;
+  if (!workspace) return DSLPG_ERR_NULL_POINTER;
+  const int64_t rb = N * dtype_size(x_dtype);
+  return host_rows_pipeline(x_host, y_host, M, rb, rb, workspace, workspace_bytes, stream,
+                            [&](void* in, void* out, int64_t rows, cudaStream_t st) {
+                              return dslpg_layer_norm_fwd(in, weight, bias, out, rows, N, x_dtype, w_dtype, eps, st);
                             });
 }

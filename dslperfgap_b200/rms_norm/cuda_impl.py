@@ -5,7 +5,6 @@ Same signature as ViperBench/rms_norm/pytorch_impl.py:3-10:
 ``(x.float() / sqrt(mean(x.float()**2) + eps) * weight.float()).to(x.dtype)``
 over the trailing ``len(normalized_shape)`` dims, in one kernel.
 """
-import ctypes
 import math
 
 import torch
@@ -69,14 +68,5 @@ def rms_norm_host(x, normalized_shape, weight, eps=1e-5, out=None):
     if x.numel() == 0:
         return out
     w = weight.contiguous()
-    lib = _lib.load()
-    need = ctypes.c_int64(0)
-    _lib.check(lib.dslpg_rms_norm_fwd_host_workspace_bytes(m, n, xc, ctypes.byref(need)), "workspace_bytes")
-    with torch.cuda.device(dev):
-        ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
-        stream = torch.cuda.current_stream(dev)
-        rc = lib.dslpg_rms_norm_fwd_host(x.data_ptr(), w.data_ptr(), out.data_ptr(), m, n, xc, wc, float(eps),
-                                         ws.data_ptr(), need.value, stream.cuda_stream)
-        _lib.check(rc, "dslpg_rms_norm_fwd_host")
-        stream.synchronize()
+    _lib.run_host_pipeline("dslpg_rms_norm_fwd_host", x, out, dev, m, n, xc, (w.data_ptr(),), (wc, float(eps)))
     return out

@@ -239,6 +239,19 @@ DSLPG_API int dslpg_rms_norm_fwd_host(const void* x_host, const void* weight, vo
                                       cudaStream_t stream);
 
 /*
+ * dslpg_layer_norm_fwd on HOST buffers, with the same chunked pipeline,
+ * workspace rule and ordering as dslpg_rms_norm_fwd_host above; weight and
+ * bias (bias may be NULL) are device pointers. Same result as
+ * dslpg_layer_norm_fwd row by row. Serves the reference's layer_norm
+ * (ViperBench/layer_norm/pytorch_impl.py:5-12) for inputs that live in host
+ * memory, e.g. one row block per GPU of a batch held by the host.
+ */
+DSLPG_API int dslpg_layer_norm_fwd_host_workspace_bytes(int64_t M, int64_t N, int x_dtype, int64_t* bytes);
+DSLPG_API int dslpg_layer_norm_fwd_host(const void* x_host, const void* weight, const void* bias, void* y_host,
+                                        int64_t M, int64_t N, int x_dtype, int w_dtype, float eps, void* workspace,
+                                        int64_t workspace_bytes, cudaStream_t stream);
+
+/*
  * Llama feed-forward with the RMSNorm fused around a dual GEMM (tcgen05 tensor
  * cores; for M <= 3 rows a kernel that streams the weight rows instead):
  *   a_norm[m] = rsqrt(sum_k x[m,k]^2 / K + 1e-6);  xs = x * rms_w (fp16);

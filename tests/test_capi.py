@@ -85,6 +85,15 @@ def test_argument_errors_return_before_launch(lib):
     assert need.value == 4 * 2 * (16 << 20)  # 4 slots of a 16 MiB input chunk and its output chunk
     assert lib.dslpg_rms_norm_fwd_host_workspace_bytes(3, 5, 0, ctypes.byref(need)) == 0 and need.value == 4 * 2 * 256
     assert lib.dslpg_rms_norm_fwd_host(8, 8, 8, 4, 4, 2, 2, 1e-6, 256, need.value - 1, None) == -5  # too small
+    # host-buffer layer_norm: the same checks (bias may be NULL), the same workspace rule
+    assert lib.dslpg_layer_norm_fwd_host(None, 8, None, 8, 4, 4, 2, 2, 1e-5, 8, 1 << 30, None) == -1
+    assert lib.dslpg_layer_norm_fwd_host(8, 8, None, 8, 4, 4, 2, 5, 1e-5, 8, 1 << 30, None) == -3
+    assert lib.dslpg_layer_norm_fwd_host(8, 8, None, 8, 4, 4, 2, 2, float("nan"), 8, 1 << 30, None) == -4
+    assert lib.dslpg_layer_norm_fwd_host(8, 8, 8, 8, 4, 4, 2, 2, 1e-5, None, 1 << 30, None) == -1
+    need2 = ctypes.c_int64(-1)
+    assert lib.dslpg_layer_norm_fwd_host_workspace_bytes(131072, 8192, 2, ctypes.byref(need2)) == 0
+    assert need2.value == 4 * 2 * (16 << 20)
+    assert lib.dslpg_layer_norm_fwd_host(8, 8, 8, 8, 4, 4, 2, 2, 1e-5, 256, need.value - 1, None) == -5
     # kernel_ff: K % 8, the workspace size, and the static-scratch variant's limit (checked before M * K is formed)
     assert lib.dslpg_kernel_ff(8, 8, 8, 8, 8, 4, 4, 12, 256, 1 << 20, None) == -2
     assert lib.dslpg_kernel_ff(8, 8, 8, 8, 8, 4, 4, 16, 256, 1, None) == -5

@@ -1,7 +1,8 @@
-"""Row-sharded execution on two GPUs over NCCL: each rank runs the CUDA
-kernels on its row block of a configuration, the blocks are gathered over
-NVLink and compared with the oracle on the whole batch. Skipped on a box with
-fewer than two GPUs."""
+"""Row-sharded execution on 2, 4 and 8 GPUs over NCCL: each rank runs the
+CUDA kernels on its row block of a configuration (device buffers, and host
+buffers through layer_norm_host as the bench's e2e leg does), the blocks are
+gathered over NVLink and compared with the oracle on the whole batch. A world
+size larger than the box's GPU count is skipped."""
 import os
 import socket
 
@@ -30,33 +31,40 @@ def _worker(rank, world, port, out_q):
         r0, r1 = sharded.shard_rows(rows, rank, world)
         wl = workloads.make("layer_norm_bf16_sharded", seed=0, rows=(r0, r1)).to("cuda")
         y = B.layer_norm(*wl.args, **wl.kwargs)
+        x, w, b = wl.args
+        y_host = B.layer_norm_host(x.cpu().pin_memory(), w, b)
+        host_ok = torch.tensor([int(torch.equal(y_host.cuda(), y))], device="cuda")
+        dist.all_reduce(host_ok, op=dist.ReduceOp.MIN)
         full = sharded.gather_rows(y)
         ce = workloads.make("cross_entropy_bf16", seed=0, rows=sharded.shard_rows(64, rank, world)).to("cuda")
         loss, _, _ = B.cross_entropy_fwd(*ce.args, **ce.kwargs)
         mean = sharded.cross_entropy_mean(loss, ce.args[1], -100)
         if rank == 0:
-            out_q.put((full.cpu(), mean))
+            out_q.put((full.cpu(), mean, bool(host_ok.item())))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_sharded_layer_norm_and_mean_loss():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_layer_norm_and_mean_loss(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import parity
     from oracle import oracle
     from dslperfgap_b200 import workloads
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    full, mean = q.get(timeout=600)
+    full, mean, host_ok = q.get(timeout=600)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     wl = workloads.make("layer_norm_bf16_sharded", seed=0, rows=(0, 1024))
+    assert host_ok, "layer_norm_host differs from the device path on some rank"
     ok, msg = parity.compare(full, oracle.layer_norm(*wl.args, **wl.kwargs), torch.bfloat16, normalised=True)
     assert ok, msg
     ce = workloads.make("cross_entropy_bf16", seed=0, rows=(0, 64))
