@@ -57,6 +57,7 @@ SIGNATURES = {
     "dslpg_kernel_ff_static": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp],
     "dslpg_version": [],
     "dslpg_set_kernel_path": [_c_int],
+    "dslpg_get_kernel_path": [],
 }
 
 PATHS = {"auto": 0, "resident": 1, "tma": 2, "stream": 3, "cluster": 4}
@@ -174,8 +175,8 @@ def launch(dev: torch.device, name: str, *args) -> None:
 
 class kernel_path:
     """Context manager forcing one kernel shape ("auto", "resident", "tma",
-    "stream") for the calls made inside it (process-wide; for tests and
-    benchmarks)."""
+    "stream", "cluster") for the calls this host thread makes inside it (the
+    selection is per thread; for tests and benchmarks)."""
 
     def __init__(self, name: str):
         self.code = PATHS[name]

@@ -28,7 +28,9 @@ struct OccKeyHash {
   }
 };
 std::mutex g_occ_mu;
-std::atomic<int> g_path{DSLPG_PATH_AUTO};
+// The kernel-shape override of dslpg_set_kernel_path: per host thread, so a
+// test or benchmark that forces one shape never changes another thread's launches.
+thread_local int g_path = DSLPG_PATH_AUTO;
 struct SmemKey {
   int dev;
   const void* fn;
@@ -74,6 +76,27 @@ int persistent_grid(const void* kernel, int block, size_t smem, int64_t work_cta
   return static_cast<int>(work_ctas < full ? work_ctas : full);
 }
 
+int max_active_clusters(const void* kernel, const cudaLaunchConfig_t& cfg, int cluster_size, int fallback) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  // cached beside the occupancy figures; a negative block field marks a cluster count
+  const OccKey key{dev, kernel, -(cluster_size * 4096 + static_cast<int>(cfg.blockDim.x)), cfg.dynamicSmemBytes};
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = fallback;
+  }
+  if (n < 1) n = 1;
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  g_occ[key] = n;
+  return n;
+}
+
 cudaError_t allow_dynamic_smem(const void* kernel, size_t bytes) {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -92,15 +115,17 @@ cudaError_t allow_dynamic_smem(const void* kernel, size_t bytes) {
   return e;
 }
 
-int kernel_path() { return g_path.load(std::memory_order_relaxed); }
+int kernel_path() { return g_path; }
 
 }  // namespace dslpg
 
 extern "C" int dslpg_set_kernel_path(int path) {
   if (path < DSLPG_PATH_AUTO || path > DSLPG_PATH_CLUSTER) return DSLPG_ERR_BAD_ARGUMENT;
-  dslpg::g_path.store(path);
+  dslpg::g_path = path;
   return DSLPG_OK;
 }
+
+extern "C" int dslpg_get_kernel_path(void) { return dslpg::g_path; }
 
 extern "C" unsigned int dslpg_take_wait_timeouts(void) {
   return dslpg::take_wait_timeouts_rownorm() + dslpg::take_wait_timeouts_rowstat() + dslpg::take_wait_timeouts_ff();

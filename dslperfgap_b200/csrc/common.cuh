@@ -418,6 +418,10 @@ int persistent_grid(const void* kernel, int block, size_t smem, int64_t work_cta
 
 // Allow `kernel` to use `bytes` of dynamic shared memory (cached per device).
 cudaError_t allow_dynamic_smem(const void* kernel, size_t bytes);
+// Co-resident clusters of `cluster_size` CTAs for launch configuration `cfg`
+// (cudaOccupancyMaxActiveClusters), cached per device, kernel, block and shared
+// memory under the occupancy cache's lock; `fallback` when the query fails.
+int max_active_clusters(const void* kernel, const cudaLaunchConfig_t& cfg, int cluster_size, int fallback);
 
 // Kernel-shape override (DSLPG_PATH_*), set by dslpg_set_kernel_path.
 int kernel_path();

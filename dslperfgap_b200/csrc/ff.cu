@@ -827,12 +827,8 @@ extern "C" int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, co
     cfg.dynamicSmemBytes = kFfSmem2;
     cfg.stream = stream;
     cfg.gridDim = dim3(2);
-    static int max_pairs = 0;  // co-resident CTA pairs (same device model for every device used)
-    if (max_pairs == 0) {
-      int n = 0;
-      if (cudaError_t e = cudaOccupancyMaxActiveClusters(&n, ff_gemm2_kernel, &cfg)) return static_cast<int>(e);
-      max_pairs = n > 0 ? n : 1;
-    }
+    // co-resident CTA pairs on this device (cached per device with the occupancy figures)
+    const int max_pairs = max_active_clusters(fn, cfg, 2, sm_count() / 2);
     cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min<int64_t>(tiles, max_pairs)));
     return static_cast<int>(cudaLaunchKernelEx(&cfg, ff_gemm2_kernel, ma, mb1, mb3, args));
   }
@@ -858,25 +854,60 @@ constexpr int64_t kStaticScratchBytes = DSLPG_KERNEL_FF_STATIC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_ff_scratch[kStaticScratchBytes];
 
 constexpr int kMaxDevices = 64;
-std::atomic<void*> g_scratch_addr[kMaxDevices];
+struct ScratchAddr {
+  unsigned long long ctx_id = 0;  // the CUDA context the address belongs to (0: none yet)
+  void* addr = nullptr;
+};
+ScratchAddr g_scratch_addr[kMaxDevices];
 std::mutex g_scratch_mu;
 
-// The scratch's device address on the current device, looked up once per
-// device (with that device current) by the first call there.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// The unique id of the calling thread's current CUDA context (0 when it cannot
+// be read). A device reset or a new primary context gets a new id, which is
+// what makes a cached scratch address stale.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) ? reinterpret_cast<CtxGetCurrentFn>(p) : nullptr;
+  }();
+  static CtxGetIdFn get_id = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) ? reinterpret_cast<CtxGetIdFn>(p) : nullptr;
+  }();
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// The scratch's device address in the current device's current context. The
+// lookup (cudaGetSymbolAddress, with that device current) is the set-up step:
+// it runs on the first call on each device, and again only after the device's
+// context has been replaced (for example after cudaDeviceReset), since the
+// module's addresses belong to the context that loaded it.
 cudaError_t static_scratch(void** out) {
   int dev = 0;
   if (cudaError_t e = cudaGetDevice(&dev)) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    p = g_scratch_addr[dev].load(std::memory_order_relaxed);
-    if (p == nullptr) {
-      if (cudaError_t e = cudaGetSymbolAddress(&p, g_ff_scratch)) return e;
-      g_scratch_addr[dev].store(p, std::memory_order_release);
-    }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  ScratchAddr& slot = g_scratch_addr[dev];
+  unsigned long long id = current_context_id();
+  if (slot.addr == nullptr || id == 0 || slot.ctx_id != id) {
+    void* p = nullptr;
+    if (cudaError_t e = cudaGetSymbolAddress(&p, g_ff_scratch)) return e;
+    if (id == 0) id = current_context_id();  // the lookup made the context current
+    slot.addr = p;
+    slot.ctx_id = id;
   }
-  *out = p;
+  *out = slot.addr;
   return cudaSuccess;
 }
 }  // namespace

@@ -764,13 +764,8 @@ cudaError_t launch_cluster_v(RowArgs a, int C, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3(C * sm_count());
-  int max_clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&max_clusters, cluster_norm_kernel<OP, Tin, Tout, VPT>, &cfg) != cudaSuccess ||
-      max_clusters < 1) {
-    cudaGetLastError();
-    max_clusters = sm_count() / C;
-  }
-  if (max_clusters < 1) max_clusters = 1;
+  const int max_clusters = max_active_clusters(
+      reinterpret_cast<const void*>(&cluster_norm_kernel<OP, Tin, Tout, VPT>), cfg, C, sm_count() / C);
   const int64_t nclusters = a.M < max_clusters ? a.M : max_clusters;
   cfg.gridDim = dim3(static_cast<unsigned>(nclusters * C));
   return cudaLaunchKernelEx(&cfg, cluster_norm_kernel<OP, Tin, Tout, VPT>, a, slice_vecs);

@@ -625,13 +625,8 @@ cudaError_t launch_cluster_stat(StatArgs a, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3(static_cast<unsigned>(C * sm_count()));
-  int max_clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&max_clusters, cluster_stat_kernel<KIND, T, SMOOTH>, &cfg) != cudaSuccess ||
-      max_clusters < 1) {
-    cudaGetLastError();
-    max_clusters = static_cast<int>(sm_count() / C);
-  }
-  if (max_clusters < 1) max_clusters = 1;
+  const int max_clusters = max_active_clusters(reinterpret_cast<const void*>(&cluster_stat_kernel<KIND, T, SMOOTH>),
+                                               cfg, static_cast<int>(C), static_cast<int>(sm_count() / C));
   const int64_t nclusters = items < max_clusters ? items : max_clusters;
   cfg.gridDim = dim3(static_cast<unsigned>(nclusters * C));
   return cudaLaunchKernelEx(&cfg, cluster_stat_kernel<KIND, T, SMOOTH>, a, slice_vecs);

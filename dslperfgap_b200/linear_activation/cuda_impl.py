@@ -15,6 +15,11 @@ import torch
 from .. import _lib
 
 
+def _aligned16(t):
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def kernel_ff(x, w1, w3, rms_w):
     dev = _lib.require_cuda(x, w1, w3, rms_w, what="kernel_ff")
     x = x.half() if x.dtype != torch.float16 else x
@@ -23,7 +28,8 @@ def kernel_ff(x, w1, w3, rms_w):
     rms_w = rms_w.half() if rms_w.dtype != torch.float16 else rms_w
     if x.dim() != 3:
         raise ValueError(f"kernel_ff: x must be [batch, seq_len, dim], got {tuple(x.shape)}")
-    assert w1.shape == w3.shape
+    if w1.shape != w3.shape:
+        raise ValueError(f"kernel_ff: w1 {tuple(w1.shape)} and w3 {tuple(w3.shape)} differ in shape")
     batch, seq_len, dim = x.shape
     n = w1.shape[0]
     if w1.shape[1] != dim or rms_w.numel() != dim:
@@ -31,8 +37,10 @@ def kernel_ff(x, w1, w3, rms_w):
     if dim % 8 != 0:
         raise ValueError(f"kernel_ff: dim must be a multiple of 8 (16-byte rows), got {dim}")
     m = batch * seq_len
-    xf = x.reshape(m, dim).contiguous()
-    w1c, w3c, rw = w1.contiguous(), w3.contiguous(), rms_w.contiguous()
+    # the kernels read 16-byte vectors and TMA tiles: a contiguous view at an odd
+    # offset (e.g. sliced from a flat parameter buffer) is copied to a fresh,
+    # 256-byte aligned allocation
+    xf, w1c, w3c, rw = (_aligned16(t) for t in (x.reshape(m, dim), w1, w3, rms_w.reshape(dim)))
     out = torch.empty((m, n), dtype=torch.float16, device=x.device)
     if m == 0 or n == 0:
         return out.view(batch, seq_len, n)

@@ -6,7 +6,9 @@
  * and returns 0 on success, a positive cudaError_t when a CUDA call failed, or
  * a negative DSLPG_ERR_* code when the arguments were rejected before any
  * launch. No entry point allocates memory, synchronises, or keeps state other
- * than a per-device cache of SM counts and occupancy figures.
+ * than a per-device cache of SM counts and occupancy figures (lock-protected),
+ * the per-thread kernel-shape selection below, and the per-device copy streams
+ * of the host-buffer entry points.
  *
  * Layout: every row-wise operand is a dense row-major [M, N] matrix (the
  * reference flattens x[..., D] to [M, D] the same way). The caller owns every
@@ -69,10 +71,15 @@ enum {
                               kernel_ff: CTA pairs (tcgen05 cta_group::2) on 256x128 tiles */
 };
 
-/* Select the kernel shape for subsequent calls (process-wide). A path that
- * cannot handle a given shape falls back to one that can. Returns 0 or
- * DSLPG_ERR_BAD_ARGUMENT. No reference counterpart: a testing aid. */
+/* Select the kernel shape for the calling host thread's subsequent calls
+ * (a per-thread setting: other threads keep their own, DSLPG_PATH_AUTO unless
+ * they set one). A path that cannot handle a given shape falls back to one
+ * that can. Returns 0 or DSLPG_ERR_BAD_ARGUMENT. No reference counterpart: a
+ * testing aid. */
 DSLPG_API int dslpg_set_kernel_path(int path);
+
+/* The calling thread's kernel-shape selection. No reference counterpart. */
+DSLPG_API int dslpg_get_kernel_path(void);
 
 /* Number of bounded device-side waits (TMA pipeline barriers) that ran out of
  * time since the last call, and reset the count. Synchronises the device.
@@ -278,7 +285,13 @@ DSLPG_API int dslpg_kernel_ff(const void* x, const void* w1, const void* w3, con
  * synchronisation of cudaMalloc / cudaFree is not acceptable.
  * Set-up: the first call on each device (the device current at the call) looks
  * up the scratch address with cudaGetSymbolAddress, which may load this
- * library's device code; make that first call before any stream capture.
+ * library's device code; make that first call before any stream capture. The
+ * address is kept per device together with the id of the CUDA context it
+ * belongs to, so after a cudaDeviceReset (or any replacement of the device's
+ * context) the next call repeats the set-up instead of using a stale address.
+ * The scratch is part of this library's device code: once any kernel_ff entry
+ * point has loaded that code on a device, its 16 MiB + 64 KiB stay allocated
+ * there until the context ends, also for callers that only use dslpg_kernel_ff.
  * No part of the scratch has to start at zero (every call writes all of xs and
  * a_norm before reading them). There is ONE scratch per device: calls that
  * overlap on the same device (different streams, or different host threads

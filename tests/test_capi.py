@@ -40,6 +40,25 @@ def test_python_binding_covers_header():
     assert set(declared_symbols()) <= bound
 
 
+def test_kernel_path_is_per_thread(lib):
+    """A shape forced on one host thread does not reach another thread's calls."""
+    import threading
+    seen = {}
+    lib.dslpg_set_kernel_path(3)
+    try:
+        def other():
+            seen["before"] = lib.dslpg_get_kernel_path()
+            lib.dslpg_set_kernel_path(1)
+            seen["after"] = lib.dslpg_get_kernel_path()
+        t = threading.Thread(target=other)
+        t.start()
+        t.join()
+        assert seen == {"before": 0, "after": 1}
+        assert lib.dslpg_get_kernel_path() == 3
+    finally:
+        lib.dslpg_set_kernel_path(0)
+
+
 def test_kernel_path_validation(lib):
     assert lib.dslpg_set_kernel_path(9) == -5
     assert lib.dslpg_set_kernel_path(-1) == -5

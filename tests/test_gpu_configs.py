@@ -39,8 +39,12 @@ def test_full_size_config_matches_oracle(name):
     elif not ref.dtype.is_floating_point:  # argmax
         assert torch.equal(out.cpu(), ref)
     elif wl.op == "linear_activation":  # fp32 dot products of length K before the gate
-        ok, msg = parity.compare(out, ref, wl.out_dtype, abs_slack=parity.GEMM_SLACK * ref.float().abs().max().item())
+        ok, msg = parity.compare(out, ref, wl.out_dtype, abs_slack=parity.gemm_slack(*wl.args))
         assert ok, msg
+        hist = parity.ulp_histogram(out, ref, wl.out_dtype)
+        print(f"kernel_ff {wl.M}x{wl.config.K} @ {wl.config.N}: |out - ref| in fp16 ulps {hist}")
+        within1 = hist["[0,0.5]"] + hist["(0.5,1]"]
+        assert within1 >= 0.99 * out.numel(), hist  # the slack is for the cancelling few
     else:
         assert_parity(out, ref, wl.out_dtype, normalised=wl.op in parity.NORMALISED)
 

@@ -428,5 +428,24 @@ def test_kernel_ff(b, s, d, n, path):
     ref = oracle.kernel_ff(x, w1, w3, rw)
     assert _lib.take_wait_timeouts() == 0
     assert out.shape == ref.shape and out.dtype == torch.float16
-    ok, msg = parity.compare(out, ref, torch.float16, abs_slack=parity.GEMM_SLACK * ref.float().abs().max().item())
+    ok, msg = parity.compare(out, ref, torch.float16, abs_slack=parity.gemm_slack(x, w1, w3, rw))
+    assert ok, msg
+
+
+def test_kernel_ff_misaligned_views():
+    """A contiguous view at an odd offset (rms_w sliced from a flat fp16
+    parameter buffer) is accepted, as the reference accepts it."""
+    g = gen(77)
+    d, n = 512, 384
+    x = randn((1, 64, d), torch.float16, g)
+    w1 = randn((n, d), torch.float16, g, std=d ** -0.5)
+    w3 = randn((n, d), torch.float16, g, std=d ** -0.5)
+    rw = randn((d,), torch.float16, g, mean=1.0, std=0.1)
+    flat = torch.empty(d + 3, dtype=torch.float16, device="cuda")
+    flat[3:] = rw.cuda()
+    rw_view = flat[3:]
+    assert rw_view.data_ptr() % 16 != 0 and rw_view.is_contiguous()
+    out = B.kernel_ff(x.cuda(), w1.cuda(), w3.cuda(), rw_view)
+    ok, msg = parity.compare(out, oracle.kernel_ff(x, w1, w3, rw), torch.float16,
+                             abs_slack=parity.gemm_slack(x, w1, w3, rw))
     assert ok, msg

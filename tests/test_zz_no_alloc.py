@@ -58,7 +58,10 @@ def test_static_scratch_matches_workspace_entry_on_two_calls():
     lib = _lib.load()
     # first call: a large problem; second call: a smaller one whose xs covers
     # only part of what the first call left in the scratch
-    for seed, (m, k, n) in [(11, (1000, 2048, 1536)), (12, (333, 320, 1000))]:
+    # then decode-like rows (the weight-streaming kernel, a_norm placed right
+    # after a tiny xs) over what the larger calls left behind
+    for seed, (m, k, n) in [(11, (1000, 2048, 1536)), (12, (333, 320, 1000)), (15, (1, 4096, 1000)),
+                            (16, (3, 4096, 1000))]:
         args = inputs(seed, m, k, n)
         ref = with_workspace(lib, *args)
         rc, out = static(lib, *args)
