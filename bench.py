@@ -681,6 +681,9 @@ PUBLISHED = {
 
 
 def reference_protocol_ms(fn, warmup=10, iters=100):
+    """ViperBench/benchmark.py:26-58: median of `iters` calls, each bracketed by
+    torch.cuda.synchronize() and perf_counter, after `warmup` calls; then the
+    peak allocated memory (MB) of one more call."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -692,7 +695,44 @@ def reference_protocol_ms(fn, warmup=10, iters=100):
         torch.cuda.synchronize()
         times.append((time.perf_counter() - t0) * 1000)
     times.sort()
-    return times[len(times) // 2]
+    torch.cuda.reset_peak_memory_stats()
+    torch.cuda.synchronize()
+    fn()
+    torch.cuda.synchronize()
+    return times[len(times) // 2], torch.cuda.max_memory_allocated() / (1024 * 1024)
+
+
+def eager_cross_entropy_fwd(logits, labels, logit_scale, lse_square_scale, ignored_index, class_start_idx, block):
+    """The reference's own GPU baseline for cross_entropy_fwd without smoothing
+    or SPLIT: the vectorised torch expression of
+    ViperBench/cross_entropy/pytorch_impl.py:21-90 (per-block lse over -inf
+    padded fp32 blocks, label term where the label falls in the block, the
+    kernel's flat [block * n_rows + row] layout in [n_rows, n_cols] buffers)."""
+    n_rows, n_cols = logits.shape
+    dev = logits.device
+    nb = (n_cols + block - 1) // block
+    pad = torch.full((n_rows, nb * block), float("-inf"), dtype=torch.float32, device=dev)
+    pad[:, :n_cols] = logits.float() * logit_scale
+    lb = pad.view(n_rows, nb, block)
+    mx = lb.max(dim=2).values
+    lse = torch.log(torch.exp(lb - mx.unsqueeze(2)).sum(dim=2)) + mx
+    lab = labels.to(torch.int64) - class_start_idx
+    start = torch.arange(nb, device=dev) * block
+    end = torch.clamp(start + block, max=n_cols)
+    inb = (lab.unsqueeze(1) >= start) & (lab.unsqueeze(1) < end)
+    ll = logits.gather(1, lab.clamp(0, n_cols - 1).unsqueeze(1)).float().squeeze(1) * logit_scale
+    z = lse_square_scale * lse * lse
+    loss = torch.where(inb, lse - ll.unsqueeze(1), torch.zeros_like(lse)) + z
+    keep = (labels != ignored_index).unsqueeze(1)
+    loss = torch.where(keep, loss, torch.zeros_like(loss))
+    z = torch.where(keep, z, torch.zeros_like(z))
+
+    def layout(mat):
+        flat = mat.transpose(0, 1).reshape(-1)
+        out = torch.zeros(n_rows * n_cols, dtype=torch.float32, device=dev)
+        out[: flat.numel()] = flat
+        return out.reshape(n_rows, n_cols)
+    return layout(loss), layout(lse), layout(z)
 
 
 def reference_shapes(dev):
@@ -705,53 +745,61 @@ def reference_shapes(dev):
 
     out = {}
 
-    def case(name, ours, lib, lib_name):
+    def case(name, size, ours, lib, lib_name, pyimpl=None):
+        """`pyimpl`: the reference's pytorch_impl computation where it is not
+        the library op `lib` itself (its profile.csv "pytorch" row)."""
         hw, line, (pt, tr, tl) = PUBLISHED[name]
-        ms = reference_protocol_ms(ours)
-        lib_ms = reference_protocol_ms(lib)
+        ms, mem = reference_protocol_ms(ours)
+        lib_ms, lib_mem = reference_protocol_ms(lib)
+        py_ms, py_mem = reference_protocol_ms(pyimpl) if pyimpl is not None else (lib_ms, lib_mem)
         src = "GH200-480GB" if hw == "GH200" else hw
-        out[name] = {"ms": round(ms, 4), "torch_op": lib_name, "torch_ms": round(lib_ms, 4),
-                     "e_lib_pct": round(100 * lib_ms / ms, 1),
+        out[name] = {"size": size, "ms": round(ms, 4), "peak_memory_mb": round(mem, 2), "torch_op": lib_name,
+                     "torch_ms": round(lib_ms, 4), "e_lib_pct": round(100 * lib_ms / ms, 1),
+                     "pytorch_impl_ms": round(py_ms, 4), "pytorch_impl_peak_memory_mb": round(py_mem, 2),
+                     "e_lib_vs_pytorch_impl_pct": round(100 * py_ms / ms, 1),
                      "published_ms": {"hardware": hw, "pytorch": pt, "triton": tr, "tilelang": tl,
                                       "source": f"ViperBench/results/profile.{src}.csv:{line}"}}
 
-    for m, n in ((8192, 8192), (512, 1024)):
+    for (m, n), size in (((8192, 8192), "large"), ((512, 1024), "small")):
         x = rn(m, n, dtype=torch.bfloat16)
         w, b = rn(n, dtype=torch.bfloat16), rn(n, dtype=torch.bfloat16)
-        case(f"layer_norm x:({m},{n}) bf16", lambda: B.layer_norm(x, w, b),
+        case(f"layer_norm x:({m},{n}) bf16", size, lambda: B.layer_norm(x, w, b),
              lambda: F.layer_norm(x, (n,), w, b, 1e-5), "F.layer_norm")
         x = rn(m, n, dtype=torch.float16)
         w = rn(n, dtype=torch.float16)
-        case(f"rms_norm x:({m},{n}) fp16", lambda: B.rms_norm(x, (n,), w), lambda: F.rms_norm(x, (n,), w, 1e-5),
-             "F.rms_norm")
-    for m, n in ((4096, 32768), (512, 1024)):
+        case(f"rms_norm x:({m},{n}) fp16", size, lambda: B.rms_norm(x, (n,), w), lambda: F.rms_norm(x, (n,), w, 1e-5),
+             "F.rms_norm",
+             lambda: ((x.float() / torch.sqrt(torch.mean(x.float() ** 2, dim=-1, keepdim=True) + 1e-5))
+                      * w.float()).to(x.dtype))
+    for (m, n), size in (((4096, 32768), "large"), ((512, 1024), "small")):
         x = rn(m, n, dtype=torch.float16)
-        case(f"softmax x:({m},{n}) fp16", lambda: B.softmax(x), lambda: F.softmax(x, -1), "F.softmax")
-        case(f"log_softmax x:({m},{n}) fp16", lambda: B.log_softmax(x), lambda: F.log_softmax(x, -1),
+        case(f"softmax x:({m},{n}) fp16", size, lambda: B.softmax(x), lambda: F.softmax(x, -1), "F.softmax")
+        case(f"log_softmax x:({m},{n}) fp16", size, lambda: B.log_softmax(x), lambda: F.log_softmax(x, -1),
              "F.log_softmax")
-    for m, n in ((8192, 16384), (512, 1024)):
+    for (m, n), size in (((8192, 16384), "large"), ((512, 1024), "small")):
         x = rn(m, n, dtype=torch.float32)
-        case(f"logsumexp x:({m},{n}) fp32", lambda: B.logsumexp(x), lambda: torch.logsumexp(x, -1),
+        case(f"logsumexp x:({m},{n}) fp32", size, lambda: B.logsumexp(x), lambda: torch.logsumexp(x, -1),
              "torch.logsumexp")
     del x
-    for m, n, bs in ((4096, 32768, 1024), (256, 1024, 256)):
+    for (m, n, bs), size in (((4096, 32768, 1024), "large"), ((256, 1024, 256), "small")):
         lg = rn(m, n, dtype=torch.float32)
         lb = torch.randint(0, n, (m,), generator=g, device=dev, dtype=torch.int64)
         ce_args = (0.0, 1.0, 0.0, -100, n, 0, bs, False, False)
-        case(f"cross_entropy logits:({m},{n}) fp32 BLOCK {bs}", lambda: B.cross_entropy_fwd(lg, lb, *ce_args),
+        case(f"cross_entropy logits:({m},{n}) fp32 BLOCK {bs}", size, lambda: B.cross_entropy_fwd(lg, lb, *ce_args),
              lambda: F.cross_entropy(lg, lb, ignore_index=-100, reduction="none"),
-             "F.cross_entropy(reduction='none')")
+             "F.cross_entropy(reduction='none')", lambda: eager_cross_entropy_fwd(lg, lb, 1.0, 0.0, -100, 0, bs))
         del lg
-    for m, n in ((8192, 32768), (1024, 1024)):
+    for (m, n), size in (((8192, 32768), "large"), ((1024, 1024), "small")):
         x = rn(m, n, dtype=torch.float16)
-        case(f"argmax x:({m},{n}) dim=1 fp16", lambda: B.argmax(x, 1), lambda: torch.argmax(x, 1), "torch.argmax")
-        case(f"max_reduction x:({m},{n}) dim=1 fp16", lambda: B.max_reduction(x, 1), lambda: torch.max(x, 1),
+        case(f"argmax x:({m},{n}) dim=1 fp16", size, lambda: B.argmax(x, 1), lambda: torch.argmax(x, 1),
+             "torch.argmax")
+        case(f"max_reduction x:({m},{n}) dim=1 fp16", size, lambda: B.max_reduction(x, 1), lambda: torch.max(x, 1),
              "torch.max(dim)")
         x = rn(m, n, dtype=torch.float32)
-        case(f"mean_reduction x:({m},{n}) dim=1 fp32", lambda: B.mean_reduction(x, 1), lambda: torch.mean(x, 1),
+        case(f"mean_reduction x:({m},{n}) dim=1 fp32", size, lambda: B.mean_reduction(x, 1), lambda: torch.mean(x, 1),
              "torch.mean")
         del x
-    for s_, k, nn in ((2048, 4096, 16384), (256, 1024, 4096)):
+    for (s_, k, nn), size in (((2048, 4096, 16384), "large"), ((256, 1024, 4096), "small")):
         x = rn(1, s_, k, dtype=torch.float16)
         w1, w3 = rn(nn, k, dtype=torch.float16), rn(nn, k, dtype=torch.float16)
         rw = rn(k, dtype=torch.float16)
@@ -761,12 +809,44 @@ def reference_shapes(dev):
             an = torch.rsqrt(xf.float().pow(2).mean(-1, keepdim=True) + 1e-6)
             xs = xf * rw
             return (F.silu((xs @ w1.t()).float() * an) * ((xs @ w3.t()).float() * an)).half()
-        case(f"linear_activation x:(1,{s_},{k}) w1/w3:({nn},{k}) fp16", lambda: B.kernel_ff(x, w1, w3, rw), ff_torch,
-             "cuBLAS fp16 GEMMs + eager epilogue")
+
+        def ff_pytorch_impl():  # ViperBench/linear_activation/pytorch_impl.py:31-54: fp32 matmuls
+            xf = x.reshape(-1, k)
+            an = torch.rsqrt((xf.float() ** 2).sum(-1) / k + 1e-6)
+            xs = (xf * rw.unsqueeze(0)).float()
+            a1 = (xs @ w1.float().T) * an.unsqueeze(1)
+            a2 = (xs @ w3.float().T) * an.unsqueeze(1)
+            return ((a1 * torch.sigmoid(a1)) * a2).half()
+        case(f"linear_activation x:(1,{s_},{k}) w1/w3:({nn},{k}) fp16", size, lambda: B.kernel_ff(x, w1, w3, rw),
+             ff_torch, "cuBLAS fp16 GEMMs + eager epilogue", ff_pytorch_impl)
         del x, w1, w3
     torch.cuda.empty_cache()
     return {"protocol": "ViperBench/benchmark.py:26-58 (perf_counter + synchronize per call, median of 100 after 10)",
             "data": "torch.randn on the device, seed 0 (the reference's shapes and distributions)", "cases": out}
+
+
+PROFILE_FIELDS = ["kernel", "size", "impl", "input_desc", "latency_ms", "peak_memory_mb"]
+
+
+def write_profile_csv(ref_shapes, path):
+    """The reference shapes as rows of ViperBench's profile.csv
+    (ViperBench/benchmark.py:443-448): impl "pytorch" is the reference's
+    pytorch_impl computation and impl "cuda" this backend, both timed here
+    with the reference's protocol; experiments/compute_elib.py reads the file
+    unchanged."""
+    import csv
+    rows = []
+    for name, c in ref_shapes["cases"].items():
+        kernel, desc = name.split(" ", 1)
+        rows.append({"kernel": kernel, "size": c["size"], "impl": "pytorch", "input_desc": desc,
+                     "latency_ms": c["pytorch_impl_ms"], "peak_memory_mb": c["pytorch_impl_peak_memory_mb"]})
+        rows.append({"kernel": kernel, "size": c["size"], "impl": "cuda", "input_desc": desc,
+                     "latency_ms": c["ms"], "peak_memory_mb": c["peak_memory_mb"]})
+    Path(path).parent.mkdir(parents=True, exist_ok=True)
+    with open(path, "w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=PROFILE_FIELDS)
+        w.writeheader()
+        w.writerows(rows)
 
 
 # ----------------------------------------------------------------- CPU baseline
@@ -879,6 +959,8 @@ def main(argv=None):
     ap.add_argument("--no-reference-shapes", action="store_true",
                     help="skip the reference's large benchmark shapes (timed with its protocol)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-csv", default=None,
+                    help="also write the reference shapes as ViperBench profile.csv rows (impl pytorch and cuda)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--path", choices=["auto", "resident", "tma", "stream"], default="auto",
                     help="force one kernel shape (default: the dispatcher's choice)")
@@ -940,6 +1022,8 @@ def main(argv=None):
     ref_shapes = None
     if world == 1 and not (args.kernel_only or args.headline_only or args.no_reference_shapes):
         ref_shapes = reference_shapes(dev)
+        if args.profile_csv:
+            write_profile_csv(ref_shapes, args.profile_csv)
 
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.kernel_only):
