@@ -130,12 +130,15 @@ def collect(out_dir: Path, targets, rows: int = 0) -> int:
         r = target_rows(name, rows)
         for letter, (tag, extra, metrics) in METRIC_SETS.items():
             out = out_dir / f"{name}_cuda_r{r}_{tag}.csv"
+            # the demangled name carries the namespace: only this library's kernels match
             cmd = [ncu_path(), "--clock-control", "none", "--target-processes", "all", "--nvtx", "--nvtx-include",
-                   "TARGET/", "--kernel-name", "regex:dslpg", "--launch-count", "1", *extra.split(),
-                   "--metrics", ",".join(metrics), "--csv", "--log-file", str(out),
+                   "TARGET/", "--kernel-name-base", "demangled", "--kernel-name", "regex:dslpg::", "--launch-count",
+                   "1", *extra.split(), "--metrics", ",".join(metrics), "--csv", "--log-file", str(out),
                    sys.executable, "-m", "dslperfgap_b200.ncu_counters", "run", name, "--rows", str(r)]
             print("[ncu_counters]", " ".join(cmd), flush=True)
             rc = subprocess.run(cmd).returncode
+            if rc == 0 and not any(r.get("Metric Name") for r in _rows(out)):
+                rc = -1  # ncu exited 0 but captured no kernel
             if rc != 0:
                 print(f"[ncu_counters] set {letter} of {name} exited {rc}", flush=True)
                 fails += 1
