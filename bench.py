@@ -22,9 +22,10 @@ public host-buffer API (`layer_norm_host`: pinned host rows in, host rows
 out, copies inside the timed region).
 
 At N = 1 every other configuration is timed too (under "kernels"), each step
-after a 512 MiB L2-flush write and bracketed by its own CUDA events, beside its
-torch GPU operator; the reference's own benchmark shapes run with its own
-protocol ("reference_shapes"). SM clocks and throttle reasons are sampled
+after an L2 flush (a 512 MiB buffer written, then half of it read back, so
+the flush's own dirty lines reach HBM before the step) and bracketed by its
+own CUDA events, beside its torch GPU operator; the reference's own benchmark
+shapes run with its own protocol ("reference_shapes"). SM clocks and throttle reasons are sampled
 (NVML, read-only) during the timed regions.
 
 --impl reference times the reference's CPU path for the same workload and
@@ -203,7 +204,12 @@ class Timer:
         self.flush_buf = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
 
     def flush(self):
+        """Evict the last step's data from L2 and leave L2 clean: write the
+        512 MiB buffer (larger than the 126 MB L2), then read its first half,
+        which pushes the written (dirty) lines out to HBM before the timed
+        step, so the step does not pay another buffer's write-backs."""
         self.flush_buf.fill_(1.0)
+        self.flush_buf[: self.flush_buf.numel() // 2].sum()
 
     def barrier(self):
         if self.world > 1:
@@ -499,6 +505,18 @@ def measure_workload(name, rank, world, dev, timer, steps, warmup, peak, sampler
             res["e_lib_pct"] = round(100.0 * t_torch / ms_step, 1)
         except Exception as e:  # report, do not hide
             res["torch_error"] = f"{type(e).__name__}: {e}"[:200]
+        if cfg.op in ("layer_norm", "rms_norm", "softmax", "log_softmax"):
+            # calibration: torch's copy_ of the same bytes (x read, a same-size
+            # buffer written) under the identical flush-then-events protocol
+            src = wl.args[0]
+            dst = torch.empty_like(src)
+            tc = timer.time_steps(lambda: dst.copy_(src), steps, warmup)
+            t_c = timer.max_over_ranks(sum(tc)) / steps
+            copy_gbs = 2 * src.numel() * src.element_size() / (t_c * 1e-3) / 1e9
+            res["copy_same_bytes_gbs"] = round(copy_gbs, 1)
+            res["copy_same_bytes_frac_measured"] = round(copy_gbs / peak, 4)
+            res["frac_of_copy_same_bytes"] = round(achieved / copy_gbs, 4)
+            del dst
         eager = eager_reference_expression(wl)
         if eager is not None:
             te = timer.time_steps(eager, steps, warmup)
@@ -1038,7 +1056,7 @@ def main(argv=None):
             l2 = ("inputs larger than L2: each rank's row block is >= 256 MiB and two copies of it alternate "
                   "between steps (no flush)")
         else:
-            l2 = "512 MiB buffer written between timed steps"
+            l2 = "L2 flush between timed steps: a 512 MiB buffer written, then its first half read back"
         line = {
             "metric": METRIC, "value": head["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
