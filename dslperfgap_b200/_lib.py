@@ -154,6 +154,46 @@ def fast_module():
     return _fast or None
 
 
+_torch_ops = None  # the _dslpg_torch extension module, or False when not used
+
+
+def torch_ops():
+    """The C++ fast path of the wrappers (csrc/torch_ops.cpp, built next to the
+    library), or None. Each of its functions returns None for a case it does
+    not take, and the Python wrapper then does the work. Not used when
+    DSLPG_LIB selects another library build (the extension is linked to the
+    default one)."""
+    global _torch_ops
+    if _torch_ops is None:
+        load()
+        mod = False
+        if not os.environ.get("DSLPG_LIB"):
+            import importlib.machinery
+            import importlib.util
+            from .build import TORCH_OPS_PATH
+            if TORCH_OPS_PATH.exists():
+                loader = importlib.machinery.ExtensionFileLoader("_dslpg_torch", str(TORCH_OPS_PATH))
+                spec = importlib.util.spec_from_file_location("_dslpg_torch", str(TORCH_OPS_PATH), loader=loader)
+                mod = importlib.util.module_from_spec(spec)
+                loader.exec_module(mod)
+        _torch_ops = mod
+    return _torch_ops or None
+
+
+def fast_op(name: str):
+    """Callable taking the wrapper's arguments and returning its result, or
+    None when the C++ fast path does not take the case (or is not built)."""
+    state = {}
+
+    def call(*args):
+        fn = state.get("fn")
+        if fn is None:
+            mod = torch_ops()
+            fn = state["fn"] = getattr(mod, name) if mod is not None else (lambda *a: None)
+        return fn(*args)
+    return call
+
+
 def launch(dev: torch.device, name: str, *args) -> None:
     """Call entry point `name`(*args, stream) on `dev` with that device's current
     stream appended; raise RuntimeError on a non-zero return. The current device

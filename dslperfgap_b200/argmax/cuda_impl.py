@@ -9,8 +9,13 @@ import torch
 
 from .. import _dims, _lib
 
+_fast_argmax = _lib.fast_op("argmax")
+
 
 def argmax(input_tensor, dim, keepdim=False):
+    out = _fast_argmax(input_tensor, dim, keepdim)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     dev = _lib.require_cuda(input_tensor, what="argmax")
     code = _lib.float_code(input_tensor, "argmax")
     shape = tuple(input_tensor.shape)

@@ -31,6 +31,7 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_NAME = "libdslpg_b200.so"
 LIB_PATH = LIB_DIR / LIB_NAME
 FAST_PATH = LIB_DIR / ("_dslpg_fast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+TORCH_OPS_PATH = LIB_DIR / ("_dslpg_torch" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 CUDA_INCLUDE = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -105,6 +106,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False, 
         os.replace(tmp, lib_path)
     if out is None:
         build_fast(force=relink or force)
+        build_torch_ops(force=relink or force)
     return lib_path
 
 
@@ -123,6 +125,30 @@ def build_fast(force: bool = False) -> Path:
         raise RuntimeError(f"building {FAST_PATH.name} failed:\n{res.stdout}\n{res.stderr}")
     os.replace(tmp, FAST_PATH)
     return FAST_PATH
+
+
+def build_torch_ops(force: bool = False) -> Path:
+    """Compile csrc/torch_ops.cpp (the C++ fast path of the Python wrappers)
+    against torch's headers and libraries into lib/_dslpg_torch*.so."""
+    src = CSRC / "torch_ops.cpp"
+    if not force and TORCH_OPS_PATH.exists() and TORCH_OPS_PATH.stat().st_mtime >= max(
+            src.stat().st_mtime, LIB_PATH.stat().st_mtime, _newest_header_mtime()):
+        return TORCH_OPS_PATH
+    import torch
+    from torch.utils import cpp_extension
+    incs = [sysconfig.get_paths()["include"], str(INCLUDE), *cpp_extension.include_paths("cuda")]
+    tlib = cpp_extension.library_paths("cuda")[0]
+    abi = int(bool(torch._C._GLIBCXX_USE_CXX11_ABI))
+    tmp = TORCH_OPS_PATH.parent / (TORCH_OPS_PATH.name + ".tmp")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_dslpg_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           *[f"-I{i}" for i in incs], str(src), "-o", str(tmp), "-L", tlib, "-lc10", "-lc10_cuda", "-ltorch",
+           "-ltorch_cpu", "-ltorch_python", "-L", str(LIB_DIR), "-ldslpg_b200", "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"building {TORCH_OPS_PATH.name} failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, TORCH_OPS_PATH)
+    return TORCH_OPS_PATH
 
 
 def main(argv=None) -> int:

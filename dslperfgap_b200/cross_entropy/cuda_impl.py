@@ -23,11 +23,17 @@ import torch
 
 from .. import _lib
 
+_fast_cross_entropy_fwd = _lib.fast_op("cross_entropy_fwd")
+
 
 def cross_entropy_fwd(
     logits, labels, smoothing, logit_scale, lse_square_scale,
     ignored_index, total_classes, class_start_idx, BLOCK_SIZE, HAS_SMOOTHING, SPLIT
 ):
+    out = _fast_cross_entropy_fwd(logits, labels, smoothing, logit_scale, lse_square_scale, ignored_index, total_classes,
+                   class_start_idx, BLOCK_SIZE, HAS_SMOOTHING, SPLIT)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     dev = _lib.require_cuda(logits, labels, what="cross_entropy_fwd")
     lcode = _lib.float_code(logits, "cross_entropy_fwd logits")
     if logits.dim() != 2:

@@ -116,6 +116,12 @@ DSLPG_DEV float consumer_reduce(float v, float* red, int ncw) {
   return warp_reduce<Op>(r);
 }
 
+// LayerNorm row statistics: 0 = a sum, then a sum of squared deviations (two
+// exchanges); 1 = one Welford exchange; 2 = one Welford exchange, branch-free merge.
+#ifndef DSLPG_LN_STATS
+#define DSLPG_LN_STATS 1
+#endif
+
 // Welford statistics of a set of values: count, mean, and the sum of squared
 // deviations from the mean.
 struct Stat3 {
@@ -129,6 +135,16 @@ struct Stat3 {
 // hold identical results. Equal counts (the usual case: every thread holds
 // the same number of elements) take the exact halving path.
 DSLPG_DEV Stat3 stat_merge(Stat3 a, Stat3 b) {
+#if DSLPG_LN_STATS == 2
+  // branch-free: an empty side has n = 0 and contributes nothing; the
+  // approximate reciprocal keeps the mean within a few ulps
+  const float n = __fadd_rn(a.n, b.n);
+  const float r = __fdividef(1.f, fmaxf(n, 1.f));
+  const float d = __fsub_rn(b.mean, a.mean);
+  const float mean = __fmul_rn(__fadd_rn(__fmul_rn(a.n, a.mean), __fmul_rn(b.n, b.mean)), r);
+  const float w = __fmul_rn(__fmul_rn(a.n, b.n), r);
+  return Stat3{n, mean, __fadd_rn(__fadd_rn(a.m2, b.m2), __fmul_rn(__fmul_rn(d, d), w))};
+#else
   if (b.n == 0.f) return a;
   if (a.n == 0.f) return b;
   const float n = __fadd_rn(a.n, b.n);
@@ -142,6 +158,7 @@ DSLPG_DEV Stat3 stat_merge(Stat3 a, Stat3 b) {
     w = __fdiv_rn(__fmul_rn(a.n, b.n), n);
   }
   return Stat3{n, mean, __fadd_rn(__fadd_rn(a.m2, b.m2), __fmul_rn(__fmul_rn(d, d), w))};
+#endif
 }
 
 DSLPG_DEV Stat3 warp_stat(Stat3 s) {

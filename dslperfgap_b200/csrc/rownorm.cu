@@ -141,6 +141,26 @@ DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool
       store(k, y);
     }
   } else if constexpr (OP == kLayerNorm) {
+#if DSLPG_LN_STATS == 0
+    f32x2 s2 = pk2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k)
+#pragma unroll
+      for (int p = 0; p < P; ++p) s2 = add2(s2, pair(k, p));
+    const float mean = rd.template reduce<SumOp>(hsum2(s2)) * a.inv_n;
+    const f32x2 nmean2 = pk2(-mean, -mean);
+    f32x2 q2 = pk2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      if (!ok[k]) continue;
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const f32x2 d = add2(pair(k, p), nmean2);
+        q2 = fma2(d, d, q2);
+      }
+    }
+    const float var = rd.template reduce<SumOp>(hsum2(q2)) * a.inv_n;
+#else
     // This thread's (count, mean, squared deviations) from the values in its
     // registers (two passes over them), then the row's by Welford merging:
     // one exchange between the threads instead of a sum and then a sum of
@@ -153,7 +173,7 @@ DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool
 #pragma unroll
       for (int p = 0; p < P; ++p) s2 = add2(s2, pair(k, p));  // masked vectors hold zeros
     }
-    const float lmean = cnt > 0.f ? __fdiv_rn(hsum2(s2), cnt) : 0.f;
+    const float lmean = hsum2(s2) * __fdividef(1.f, fmaxf(cnt, 1.f));
     const f32x2 nl2 = pk2(-lmean, -lmean);
     f32x2 q2 = pk2(0.f, 0.f);
 #pragma unroll
@@ -169,6 +189,7 @@ DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool
     const float mean = st.mean;
     const f32x2 nmean2 = pk2(-mean, -mean);
     const float var = st.m2 * a.inv_n;
+#endif
     const float rstd = rsqrtf(var + a.eps);
     const f32x2 rstd2 = pk2(rstd, rstd);
 #pragma unroll

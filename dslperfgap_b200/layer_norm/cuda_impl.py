@@ -11,8 +11,13 @@ import torch
 
 from .. import _lib
 
+_fast_layer_norm = _lib.fast_op("layer_norm")
+
 
 def layer_norm(x, weight, bias, eps=1e-5):
+    out = _fast_layer_norm(x, weight, bias, eps)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     if eps != 1e-5:
         raise ValueError(f"Only eps=1e-5 is supported (got {eps}). "
                          "The Triton kernel hardcodes eps=1e-5.")

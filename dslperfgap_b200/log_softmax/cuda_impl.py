@@ -11,8 +11,13 @@ import torch
 
 from .. import _lib
 
+_fast_log_softmax = _lib.fast_op("log_softmax")
+
 
 def log_softmax(x, dim=-1, dtype=None):
+    out = _fast_log_softmax(x, dim, dtype)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     dev = _lib.require_cuda(x, what="log_softmax")
     in_code = _lib.float_code(x, "log_softmax")
     out_dtype = x.dtype if dtype is None else dtype

@@ -9,8 +9,13 @@ import torch
 
 from .. import _lib
 
+_fast_logsumexp = _lib.fast_op("logsumexp")
+
 
 def logsumexp(x):
+    out = _fast_logsumexp(x)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     dev = _lib.require_cuda(x, what="logsumexp")
     code = _lib.float_code(x, "logsumexp")
     x = x.contiguous()

@@ -9,8 +9,13 @@ import torch
 
 from .. import _dims, _lib
 
+_fast_max_reduction = _lib.fast_op("max_reduction")
+
 
 def max_reduction(input, dim, keepdim=False):
+    out = _fast_max_reduction(input, dim, keepdim)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     if not isinstance(input, torch.Tensor):
         raise TypeError('The input must be a torch.Tensor.')
     dev = _lib.require_cuda(input, what="max_reduction")

@@ -9,8 +9,13 @@ import torch
 
 from .. import _dims, _lib
 
+_fast_mean_reduction = _lib.fast_op("mean_reduction")
+
 
 def mean_reduction(input_tensor, dim, keepdim=False, dtype=None):
+    out = _fast_mean_reduction(input_tensor, dim, keepdim, dtype)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     dev = _lib.require_cuda(input_tensor, what="mean_reduction")
     in_code = _lib.float_code(input_tensor, "mean_reduction")
     out_dtype = input_tensor.dtype if dtype is None else dtype

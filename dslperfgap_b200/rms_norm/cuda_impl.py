@@ -11,8 +11,13 @@ import torch
 
 from .. import _lib
 
+_fast_rms_norm = _lib.fast_op("rms_norm")
+
 
 def rms_norm(x, normalized_shape, weight, eps=1e-5):
+    out = _fast_rms_norm(x, normalized_shape, weight, eps)
+    if out is not None:  # the C++ fast path took the common case
+        return out
     dev = _lib.require_cuda(x, weight, what="rms_norm")
     xc = _lib.float_code(x, "rms_norm")
     wc = _lib.float_code(weight, "rms_norm weight")

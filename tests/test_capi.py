@@ -136,3 +136,22 @@ def test_fast_binding_matches_ctypes_signatures(lib):
         assert getattr(fast, name)(*args) == -1, name
         with pytest.raises(TypeError):
             getattr(fast, name)(*args[:-1])
+
+
+def test_torch_fast_path_loads_and_declines_cpu_tensors(lib):
+    """The C++ fast path (_dslpg_torch) is built and loads; for what it does
+    not take (host tensors, dim lists, other eps) it returns None so that the
+    Python wrapper raises exactly as the reference-shaped API says."""
+    import torch
+    mod = _lib.torch_ops()
+    assert mod is not None, "the _dslpg_torch extension is not built"
+    x, w = torch.randn(4, 8), torch.ones(8)
+    assert mod.layer_norm(x, w, None, 1e-5) is None
+    assert mod.rms_norm(x, (8,), w, 1e-5) is None
+    assert mod.softmax(x) is None and mod.logsumexp(x) is None
+    assert mod.log_softmax(x, -1, None) is None
+    assert mod.mean_reduction(x, [0, 1], False, None) is None
+    assert mod.max_reduction("not a tensor", 1, False) is None
+    assert mod.argmax(x, None, False) is None
+    assert mod.cross_entropy_fwd(x, torch.zeros(4, dtype=torch.long), 0.0, 1.0, 0.0, -100, 8, 0, 8, False,
+                                 False) is None
