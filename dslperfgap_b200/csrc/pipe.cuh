@@ -116,107 +116,14 @@ DSLPG_DEV float consumer_reduce(float v, float* red, int ncw) {
   return warp_reduce<Op>(r);
 }
 
-// LayerNorm row statistics: 0 = a sum, then a sum of squared deviations (two
-// exchanges); 1 = one Welford exchange; 2 = one Welford exchange, branch-free merge.
-#ifndef DSLPG_LN_STATS
-#define DSLPG_LN_STATS 1
-#endif
-
-// Welford statistics of a set of values: count, mean, and the sum of squared
-// deviations from the mean.
-struct Stat3 {
-  float n, mean, m2;
-};
-
-// Pairwise combination of two sets' statistics (Chan, Golub and LeVeque),
-// written so that merge(a, b) and merge(b, a) give the same bits: only
-// commutative sums and products, with no fused multiply-add (the _rn
-// intrinsics are never contracted). Both lanes of a butterfly step therefore
-// hold identical results. Equal counts (the usual case: every thread holds
-// the same number of elements) take the exact halving path.
-DSLPG_DEV Stat3 stat_merge(Stat3 a, Stat3 b) {
-#if DSLPG_LN_STATS == 2
-  // branch-free: an empty side has n = 0 and contributes nothing; the
-  // approximate reciprocal keeps the mean within a few ulps
-  const float n = __fadd_rn(a.n, b.n);
-  const float r = __fdividef(1.f, fmaxf(n, 1.f));
-  const float d = __fsub_rn(b.mean, a.mean);
-  const float mean = __fmul_rn(__fadd_rn(__fmul_rn(a.n, a.mean), __fmul_rn(b.n, b.mean)), r);
-  const float w = __fmul_rn(__fmul_rn(a.n, b.n), r);
-  return Stat3{n, mean, __fadd_rn(__fadd_rn(a.m2, b.m2), __fmul_rn(__fmul_rn(d, d), w))};
-#else
-  if (b.n == 0.f) return a;
-  if (a.n == 0.f) return b;
-  const float n = __fadd_rn(a.n, b.n);
-  const float d = __fsub_rn(b.mean, a.mean);
-  float mean, w;
-  if (a.n == b.n) {
-    mean = __fmul_rn(0.5f, __fadd_rn(a.mean, b.mean));
-    w = __fmul_rn(0.5f, a.n);
-  } else {
-    mean = __fdiv_rn(__fadd_rn(__fmul_rn(a.n, a.mean), __fmul_rn(b.n, b.mean)), n);
-    w = __fdiv_rn(__fmul_rn(a.n, b.n), n);
-  }
-  return Stat3{n, mean, __fadd_rn(__fadd_rn(a.m2, b.m2), __fmul_rn(__fmul_rn(d, d), w))};
-#endif
-}
-
-DSLPG_DEV Stat3 warp_stat(Stat3 s) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const Stat3 t{__shfl_xor_sync(0xffffffffu, s.n, o), __shfl_xor_sync(0xffffffffu, s.mean, o),
-                  __shfl_xor_sync(0xffffffffu, s.m2, o)};
-    s = stat_merge(s, t);
-  }
-  return s;
-}
-
-// Statistics of a row group of `nw` warps from each thread's own: a warp
-// butterfly, one barrier, and a second butterfly over the warps' results.
-// `wred` holds 3 floats per warp of the CTA; every thread of the CTA calls this.
-DSLPG_DEV Stat3 group_stat(Stat3 s, float* wred, int nw, int first_warp) {
-  s = warp_stat(s);
-  if (nw == 1) return s;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  if (lane == 0) {
-    wred[3 * w] = s.n;
-    wred[3 * w + 1] = s.mean;
-    wred[3 * w + 2] = s.m2;
-  }
-  __syncthreads();
-  Stat3 r{0.f, 0.f, 0.f};
-  if (lane < nw) r = Stat3{wred[3 * (first_warp + lane)], wred[3 * (first_warp + lane) + 1],
-                           wred[3 * (first_warp + lane) + 2]};
-  return warp_stat(r);
-}
-
-// Row statistics through plain sum reductions (reducers without a combined
-// exchange): the mean from the sum of n_i * mean_i over `inv_n` = 1 / (row
-// length), then the pooled squared deviations about that mean.
-template <class R>
-DSLPG_DEV Stat3 stat_via_sums(R& rd, Stat3 s, float inv_n) {
-  const float mean = rd.template reduce<SumOp>(s.n * s.mean) * inv_n;
-  const float d = s.mean - mean;
-  const float m2 = rd.template reduce<SumOp>(s.m2 + s.n * d * d);
-  return Stat3{0.f, mean, m2};
-}
-
 // Reductions over the threads of a row group of the register-resident kernel.
 struct GroupReducer {
   float (*red)[32];
   int nw, first_warp, buf;
-  float (*wred)[96];  // Welford exchange, double-buffered like `red`
-  int wbuf;
   template <class Op> DSLPG_DEV float reduce(float v) {
     v = group_reduce<Op>(v, red[buf], nw, first_warp);
     buf ^= 1;
     return v;
-  }
-  // Row (mean, m2) in one exchange (the counts travel along; inv_n unused).
-  DSLPG_DEV Stat3 stat(Stat3 s, float) {
-    s = group_stat(s, wred[wbuf], nw, first_warp);
-    wbuf ^= 1;
-    return s;
   }
 };
 
@@ -229,7 +136,6 @@ struct ConsumerReducer {
     buf ^= 1;
     return v;
   }
-  DSLPG_DEV Stat3 stat(Stat3 s, float inv_n) { return stat_via_sums(*this, s, inv_n); }
 };
 
 // Reductions over a whole cluster: a CTA-wide reduction, the C per-CTA values
@@ -252,7 +158,6 @@ struct ClusterReducer {
     buf ^= 1;
     return r;
   }
-  DSLPG_DEV Stat3 stat(Stat3 s, float inv_n) { return stat_via_sums(*this, s, inv_n); }
 };
 
 // Ring bookkeeping: use number u of the ring (0, 1, 2, ...) maps to slot

@@ -141,7 +141,6 @@ DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool
       store(k, y);
     }
   } else if constexpr (OP == kLayerNorm) {
-#if DSLPG_LN_STATS == 0
     f32x2 s2 = pk2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
@@ -160,36 +159,6 @@ DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool
       }
     }
     const float var = rd.template reduce<SumOp>(hsum2(q2)) * a.inv_n;
-#else
-    // This thread's (count, mean, squared deviations) from the values in its
-    // registers (two passes over them), then the row's by Welford merging:
-    // one exchange between the threads instead of a sum and then a sum of
-    // squares.
-    float cnt = 0.f;
-    f32x2 s2 = pk2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      cnt += ok[k] ? static_cast<float>(E) : 0.f;
-#pragma unroll
-      for (int p = 0; p < P; ++p) s2 = add2(s2, pair(k, p));  // masked vectors hold zeros
-    }
-    const float lmean = hsum2(s2) * __fdividef(1.f, fmaxf(cnt, 1.f));
-    const f32x2 nl2 = pk2(-lmean, -lmean);
-    f32x2 q2 = pk2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      if (!ok[k]) continue;
-#pragma unroll
-      for (int p = 0; p < P; ++p) {
-        const f32x2 d = add2(pair(k, p), nl2);
-        q2 = fma2(d, d, q2);
-      }
-    }
-    const Stat3 st = rd.stat(Stat3{cnt, lmean, hsum2(q2)}, a.inv_n);
-    const float mean = st.mean;
-    const f32x2 nmean2 = pk2(-mean, -mean);
-    const float var = st.m2 * a.inv_n;
-#endif
     const float rstd = rsqrtf(var + a.eps);
     const f32x2 rstd2 = pk2(rstd, rstd);
 #pragma unroll
@@ -288,11 +257,10 @@ template <int OP, typename Tin, typename Tout, int VPT, int PD>
 __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
   constexpr int E = Elt<Tin>::kPerVec;
   __shared__ float red[2][32];
-  __shared__ float wred[OP == kLayerNorm ? 2 : 1][96];
 
   const int g = threadIdx.x / a.tpr;
   const int t = threadIdx.x - g * a.tpr;
-  GroupReducer rd{red, a.tpr >> 5, g * (a.tpr >> 5), 0, wred, 0};
+  GroupReducer rd{red, a.tpr >> 5, g * (a.tpr >> 5), 0};
 
   auto load_row = [&](Vec16* dst, int64_t row) {
 #pragma unroll
