@@ -82,7 +82,7 @@ DSLPG_DEV float load_any(const void* p, int64_t i, int dt) {
 // Read-once activations: do not allocate in L1 (the row is read once from HBM).
 DSLPG_DEV Vec16 ld_stream(const void* p) {
   Vec16 v;
-  asm("ld.global.nc" DSLPG_LD_HINT ".v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc" DSLPG_LD_HINT ".v4.u32 {%0,%1,%2,%3}, [%4];"
       : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
       : "l"(p));
   return v;
@@ -91,7 +91,7 @@ DSLPG_DEV Vec16 ld_stream(const void* p) {
 // Data re-read by many rows (weight / bias vectors): keep in L1.
 DSLPG_DEV Vec16 ld_keep(const void* p) {
   Vec16 v;
-  asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
       : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
       : "l"(p));
   return v;

@@ -120,10 +120,51 @@ DSLPG_DEV float consumer_reduce(float v, float* red, int ncw) {
 struct GroupReducer {
   float (*red)[32];
   int nw, first_warp, buf;
+  float (*red2)[64];  // pair sums (LayerNorm), double-buffered with their own toggle
+  int buf2;
   template <class Op> DSLPG_DEV float reduce(float v) {
     v = group_reduce<Op>(v, red[buf], nw, first_warp);
     buf ^= 1;
     return v;
+  }
+  // A reduction that only this row group's threads take part in (a branch
+  // that other groups of the CTA may skip): its barrier is the group's own
+  // named barrier (1 + group index; at most 8 groups of one warp each, which
+  // need no barrier, or 4 groups of two warps and more).
+  template <class Op> DSLPG_DEV float reduce_own(float v) {
+    v = warp_reduce<Op>(v);
+    if (nw == 1) return v;
+    float* r = red[buf];
+    buf ^= 1;
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) r[threadIdx.x >> 5] = v;
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + first_warp / nw), "r"(nw * 32) : "memory");
+    float q = lane < nw ? r[first_warp + lane] : Op::identity();
+    return warp_reduce<Op>(q);
+  }
+  // Two sums in one exchange: both values ride the same shuffles and barrier.
+  DSLPG_DEV void sum_pair(float& a, float& b) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
+    if (nw == 1) return;
+    float* r = red2[buf2];
+    buf2 ^= 1;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) {
+      r[2 * w] = a;
+      r[2 * w + 1] = b;
+    }
+    __syncthreads();
+    a = lane < nw ? r[2 * (first_warp + lane)] : 0.f;
+    b = lane < nw ? r[2 * (first_warp + lane) + 1] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      a += __shfl_xor_sync(0xffffffffu, a, o);
+      b += __shfl_xor_sync(0xffffffffu, b, o);
+    }
   }
 };
 
@@ -136,6 +177,12 @@ struct ConsumerReducer {
     buf ^= 1;
     return v;
   }
+  DSLPG_DEV void sum_pair(float& a, float& b) {
+    a = reduce<SumOp>(a);
+    b = reduce<SumOp>(b);
+  }
+  // one row per CTA or cluster: every thread takes the same branches
+  template <class Op> DSLPG_DEV float reduce_own(float v) { return reduce<Op>(v); }
 };
 
 // Reductions over a whole cluster: a CTA-wide reduction, the C per-CTA values
@@ -158,6 +205,12 @@ struct ClusterReducer {
     buf ^= 1;
     return r;
   }
+  DSLPG_DEV void sum_pair(float& a, float& b) {
+    a = reduce<SumOp>(a);
+    b = reduce<SumOp>(b);
+  }
+  // one row per CTA or cluster: every thread takes the same branches
+  template <class Op> DSLPG_DEV float reduce_own(float v) { return reduce<Op>(v); }
 };
 
 // Ring bookkeeping: use number u of the ring (0, 1, 2, ...) maps to slot

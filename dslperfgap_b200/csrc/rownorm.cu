@@ -141,24 +141,38 @@ DSLPG_DEV void normalize_row(const RowArgs& a, const Vec16 (&v)[VPT], const bool
       store(k, y);
     }
   } else if constexpr (OP == kLayerNorm) {
-    f32x2 s2 = pk2(0.f, 0.f);
+    // The sum and the sum of squares in one exchange; var = E[x^2] - mean^2
+    // is kept only where that difference cannot cancel badly (mean^2 <= 16 var:
+    // relative error below 1e-6). Other rows (a large offset against a small
+    // spread, or inf/NaN) take the exact second pass over (x - mean)^2. The
+    // test is on values every thread of the row holds, so the branch is uniform.
+    f32x2 s2 = pk2(0.f, 0.f), q2 = pk2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < VPT; ++k)
 #pragma unroll
-      for (int p = 0; p < P; ++p) s2 = add2(s2, pair(k, p));
-    const float mean = rd.template reduce<SumOp>(hsum2(s2)) * a.inv_n;
-    const f32x2 nmean2 = pk2(-mean, -mean);
-    f32x2 q2 = pk2(0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      if (!ok[k]) continue;
-#pragma unroll
       for (int p = 0; p < P; ++p) {
-        const f32x2 d = add2(pair(k, p), nmean2);
-        q2 = fma2(d, d, q2);
+        const f32x2 x = pair(k, p);  // masked vectors hold zeros
+        s2 = add2(s2, x);
+        q2 = fma2(x, x, q2);
       }
+    float sum = hsum2(s2), sq = hsum2(q2);
+    rd.sum_pair(sum, sq);
+    const float mean = sum * a.inv_n;
+    const f32x2 nmean2 = pk2(-mean, -mean);
+    float var = fmaf(sq, a.inv_n, -mean * mean);
+    if (!(mean * mean <= 16.f * var)) {
+      q2 = pk2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        if (!ok[k]) continue;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          const f32x2 d = add2(pair(k, p), nmean2);
+          q2 = fma2(d, d, q2);
+        }
+      }
+      var = rd.template reduce_own<SumOp>(hsum2(q2)) * a.inv_n;  // only this row's group is here
     }
-    const float var = rd.template reduce<SumOp>(hsum2(q2)) * a.inv_n;
     const float rstd = rsqrtf(var + a.eps);
     const f32x2 rstd2 = pk2(rstd, rstd);
 #pragma unroll
@@ -257,10 +271,11 @@ template <int OP, typename Tin, typename Tout, int VPT, int PD>
 __global__ void __launch_bounds__(1024) resident_kernel(const RowArgs a) {
   constexpr int E = Elt<Tin>::kPerVec;
   __shared__ float red[2][32];
+  __shared__ float red2[OP == kLayerNorm ? 2 : 1][64];
 
   const int g = threadIdx.x / a.tpr;
   const int t = threadIdx.x - g * a.tpr;
-  GroupReducer rd{red, a.tpr >> 5, g * (a.tpr >> 5), 0};
+  GroupReducer rd{red, a.tpr >> 5, g * (a.tpr >> 5), 0, red2, 0};
 
   auto load_row = [&](Vec16* dst, int64_t row) {
 #pragma unroll

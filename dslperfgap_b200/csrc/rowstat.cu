@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(256, MINB) rowstat_kernel(const StatArgs a) {
 // a forward followed by a backward. Pass 1 reads with an L2 evict-last policy.
 DSLPG_DEV Vec16 ld_policy(const void* p, uint64_t pol) {
   Vec16 v;
-  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
       : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
       : "l"(p), "l"(pol));
   return v;
