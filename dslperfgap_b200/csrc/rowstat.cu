@@ -324,6 +324,11 @@ constexpr int fused_threads() {
   return (SMOOTH ? 512 : 1024) / DSLPG_FUSED_CTAS;
 }
 
+// 16-byte loads in flight per thread in pass 2 (with the next chunk prefetched)
+#ifndef DSLPG_FUSED_PASS2_U
+#define DSLPG_FUSED_PASS2_U 2
+#endif
+
 template <typename T, int V, bool SMOOTH>
 __global__ void __launch_bounds__(fused_threads<SMOOTH>(), DSLPG_FUSED_CTAS) xent_fused_kernel(const FusedArgs f) {
   constexpr int U = 4;
@@ -394,9 +399,6 @@ __global__ void __launch_bounds__(fused_threads<SMOOTH>(), DSLPG_FUSED_CTAS) xen
     const float dl = (lp.label != a.ignored) ? dl_row : 0.f;
     const GradRow b =
         grad_row_consts(dl, a.scale, lse, a.lse_sq, SMOOTH, a.smoothing, a.total_classes, lp.label, a.class_start);
-#ifndef DSLPG_FUSED_PASS2_U
-#define DSLPG_FUSED_PASS2_U 4
-#endif
     grad_row<T, V, DSLPG_FUSED_PASS2_U>(xr, static_cast<T*>(f.dx) + r * f.ldo, f.nvec, a.N, b, a.scale, SMOOTH, t,
                                         kFusedThreads);
   }

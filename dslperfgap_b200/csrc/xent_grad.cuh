@@ -98,14 +98,22 @@ DSLPG_DEV void grad_row(const T* xr, T* yr, int nvec, int64_t N, const GradRow& 
                         int tpr) {
   if constexpr (V > 1) {
     const GradPairs c = grad_pairs(b, scale);
-    for (int j0 = t; j0 < nvec; j0 += U * tpr) {
-      Vec16 v[U];
+    // the next chunk's loads are issued before this chunk's math and stores
+    auto load = [&](Vec16 (&dst)[U], int j0) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int j = j0 + u * tpr;
-        v[u] = Vec16{{0u, 0u, 0u, 0u}};
-        if (j < nvec) v[u] = ld_stream(xr + static_cast<int64_t>(j) * V);
+        dst[u] = Vec16{{0u, 0u, 0u, 0u}};
+        if (j < nvec) dst[u] = ld_stream(xr + static_cast<int64_t>(j) * V);
       }
+    };
+    Vec16 nx[U];
+    load(nx, t);
+    for (int j0 = t; j0 < nvec; j0 += U * tpr) {
+      Vec16 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = nx[u];
+      if (j0 + U * tpr < nvec) load(nx, j0 + U * tpr);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int j = j0 + u * tpr;
