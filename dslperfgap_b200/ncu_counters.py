@@ -146,6 +146,8 @@ def collect(out_dir: Path, targets, rows: int = 0) -> int:
 
 
 def _rows(path: Path):
+    if not path.exists():  # ncu stopped before writing its log
+        return []
     lines = [ln for ln in path.read_text().splitlines(True) if not ln.startswith("==")]
     return list(csv.DictReader(lines)) if lines else []
 
